@@ -1,0 +1,109 @@
+"""B200 (sm_100a) drop-in for the Sparse-Marlin 2:4 sparse W4A16 operator.
+
+Python surface mirrors the reference's ``marlin`` package
+(hyeonu453/CSED499II ``kernel_experiments/sparse_marlin/src/marlin``):
+
+* :func:`mul_2_4` -- same positional arguments, tensor contract and error
+  messages as ``marlin.mul_2_4`` / ``marlin_cuda.mul_2_4``
+  (``__init__.py:45-58``, ``marlin_cuda.cpp:66-94``);
+* :mod:`csed499ii_b200.metadata_decode` -- the 3-bit metadata codec and the
+  3-bit GEMM (``metadata_decode`` extension: ``pack``, ``unpack``, ``fetch``,
+  ``matmul``).
+
+All compute runs in the in-tree CUDA library through its C ABI
+(``include/sm100_marlin.h``); nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+__all__ = ["mul_2_4", "scratch_bytes", "device_status"]
+
+
+def _stream_ptr(dev: int) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype, dev: int) -> None:
+    if not t.is_cuda or t.get_device() != dev:
+        raise RuntimeError(f"{name} must be a CUDA tensor on device {dev}")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must have dtype {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _groupsize(prob_k: int, s: torch.Tensor) -> int:
+    """Compressed group size as derived by ``marlin_cuda.cpp:74-77``."""
+    groupsize = -1 if s.size(0) == 1 else prob_k // 2 // s.size(0)
+    if groupsize != -1 and groupsize * s.size(0) != prob_k // 2:
+        raise RuntimeError(f"k={prob_k} not compatible with {s.size(0)} groups.")
+    return groupsize
+
+
+def _raise_for(err: int, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize) -> None:
+    if err == _ext.OK:
+        return
+    if err == _ext.ERR_PROB_SHAPE:
+        raise RuntimeError(
+            f"Problem (m={prob_m}, n={prob_n}, k={prob_k}) not compatible with "
+            f"thread_k={thread_k}, thread_m={thread_m}."
+        )
+    if err == _ext.ERR_KERN_SHAPE:
+        raise RuntimeError(
+            f"No kernel implementation for thread_k={thread_k}, thread_m={thread_m}, "
+            f"groupsize={groupsize}."
+        )
+    raise RuntimeError(f"sm100_marlin error {err}: {_ext.describe(err)}")
+
+
+def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bits):
+    lib = _ext.load()
+    prob_n = A.size(0)  # batch rows
+    prob_m = C.size(1)  # output features
+    prob_k = A.size(1)
+    groupsize = _groupsize(prob_k, s)
+    if workspace.numel() < prob_m // 128 * max_par:
+        raise RuntimeError(f"workspace must be of size at least {prob_m // 128 * max_par}.")
+    dev = A.get_device()
+    if dev < 0:
+        raise RuntimeError("A must be a CUDA tensor")
+    _check_cuda("A", A, torch.half, dev)
+    _check_cuda("B", B, torch.int32, dev)
+    _check_cuda("meta", meta, torch.int16 if meta_bits == 4 else torch.int32, dev)
+    _check_cuda("C", C, torch.half, dev)
+    _check_cuda("s", s, torch.half, dev)
+    _check_cuda("workspace", workspace, torch.int32, dev)
+    fn = lib.sm100_marlin_mul_2_4 if meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
+    err = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
+             prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
+             thread_m, sms, max_par)
+    _raise_for(err, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize)
+
+
+def mul_2_4(A, B, meta, C, s, workspace, thread_k=-1, thread_m=-1, sms=-1, max_par=16):
+    """FP16 x (INT4 + 2:4 sparsity) multiply into ``C`` (in place).
+
+    @A: ``torch.half`` activations ``(n, k)`` row-major (n = batch rows)
+    @B: ``torch.int`` packed weights ``(k/32, 2m)`` in Sparse-Marlin format
+    @meta: ``torch.int16`` 2:4 metadata ``(m, k/16)``
+    @C: ``torch.half`` output ``(n, m)`` row-major, written in place
+    @s: ``torch.half`` scales ``(k/128, m)`` or ``(1, m)``
+    @workspace: ``torch.int`` with at least ``m / 128 * max_par`` zero entries
+    @thread_k, @thread_m: -1 or a reference tile shape (shape checks only)
+    @sms: persistent CTAs (-1 = all SMs)
+    @max_par: as in the reference; only sizes the workspace requirement
+    """
+    _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, 4)
+
+
+def scratch_bytes(prob_m: int, prob_n: int, prob_k: int, dev: int = 0, sms: int = -1) -> int:
+    """Split-K scratch bytes the library keeps per (device, stream) for a call."""
+    return int(_ext.load().sm100_marlin_scratch_bytes(prob_m, prob_n, prob_k, dev, sms))
+
+
+def device_status(dev: int = 0) -> int:
+    """Read and clear the device status word (nonzero = a bounded wait gave up)."""
+    return _ext.device_status(dev)

@@ -1,0 +1,81 @@
+"""ctypes binding of the in-tree C-ABI library ``_lib/libsm100_marlin.so``.
+
+The library is the only compute path: if it is missing or cannot be loaded
+every operator raises (there is no CPU or PyTorch fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libsm100_marlin.so")
+
+_lock = threading.Lock()
+_lib = None
+
+_c_int = ctypes.c_int
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_size = ctypes.c_size_t
+
+# name -> (restype, argtypes); every name is declared in include/sm100_marlin.h
+SIGNATURES = {
+    "sm100_marlin_mul_2_4": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int,
+                                      _c_int, _vp, _c_int, _c_int, _c_int, _c_int]),
+    "sm100_marlin_mul_2_4_meta3": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
+                                            _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _c_int]),
+    "sm100_marlin_mul_2_4_ex": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
+                                         _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
+                                         _c_int, _vp, _size]),
+    "sm100_marlin_scratch_bytes": (_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "sm100_marlin_meta3_pack": (_c_int, [_vp, _vp, _i64, _vp, _vp]),
+    "sm100_marlin_meta3_unpack": (_c_int, [_vp, _vp, _i64, _vp]),
+    "sm100_marlin_meta3_decode_words": (_c_int, [_vp, _vp, _vp, _i64, _vp]),
+    "sm100_marlin_device_status": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
+    "sm100_marlin_error_string": (ctypes.c_char_p, [_c_int]),
+    "sm100_marlin_last_cuda_error": (ctypes.c_char_p, []),
+}
+
+OK = 0
+ERR_PROB_SHAPE = 1
+ERR_KERN_SHAPE = 2
+ERR_CUDA = 3
+
+
+def load(path: str = LIB_PATH):
+    """Load (once) and return the library; raise if it is not built."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"sm_100a library not built ({path} missing); run `python -m csed499ii_b200.build`"
+            )
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def describe(code: int) -> str:
+    lib = load()
+    msg = lib.sm100_marlin_error_string(code).decode()
+    if code == ERR_CUDA:
+        msg += ": " + lib.sm100_marlin_last_cuda_error().decode()
+    return msg
+
+
+def device_status(dev: int) -> int:
+    """Read and clear the device status word (bounded-wait timeouts)."""
+    lib = load()
+    out = ctypes.c_int(0)
+    rc = lib.sm100_marlin_device_status(dev, ctypes.byref(out))
+    if rc != OK:
+        raise RuntimeError(f"sm100_marlin_device_status failed: {describe(rc)}")
+    return out.value

@@ -1,0 +1,248 @@
+// Device primitives for the sm_100a 2:4 sparse W4A16 GEMM.
+//
+// Replaces the reference's Ampere helpers
+// (kernel_experiments/sparse_marlin/src/marlin/common/{base,mma,mem}.h):
+// cp.async / ldmatrix / unbounded lock spins become TMA bulk copies tracked by
+// mbarriers with *bounded* waits; the dequant and sparse MMA fragments are
+// written from the PTX ISA fragment layouts.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace sm100 {
+
+// ----------------------------------------------------------------------------
+// Status bits written by kernels that gave up waiting (read by the host via
+// sm100_marlin_device_status).  A kernel never traps: it records the bit and
+// runs to completion without waiting any further.
+// ----------------------------------------------------------------------------
+enum : int {
+  kStatusFullWaitTimeout = 1,   // consumer waited too long for a stage
+  kStatusEmptyWaitTimeout = 2,  // producer waited too long for a free slot
+};
+
+// Upper bound for any single wait, in nanoseconds of %globaltimer.
+constexpr unsigned long long kWaitLimitNs = 500ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar), "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of `parity` to complete.  Returns false (and leaves the
+// wait) when `*abort` is raised by another thread of the CTA or when the wait
+// exceeds kWaitLimitNs; in the latter case it raises `*abort` itself.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bulk (non-tensor) TMA copies global -> shared, completing on an mbarrier.
+// Both addresses must be 16-byte aligned and `bytes` a multiple of 16.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Named barriers for subsets of warps (id 0 is __syncthreads).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory loads
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// Four 8x8 b16 matrices; lane l supplies the row address of matrix l/8.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Two 8x8 b16 matrices (lanes 0..15 supply row addresses).
+__device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+
+// ---------------------------------------------------------------------------
+// INT4 -> fp16.  Magic-number construction (FasterTransformer's published
+// method): OR a nibble into the mantissa of 1024.0 (0x6400) to get 1024+n, or
+// 1024+16n for the high nibble of a byte, then remove the offset and the
+// symmetric zero point 8 with one half2 op.
+//   lo(q) = (n0 - 8, n4 - 8)     hi(q) = (n1 - 8, n5 - 8)
+// where n_i is nibble i of q.
+// ---------------------------------------------------------------------------
+template <int LUT>
+__device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm volatile("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(r) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+  return r;
+}
+
+constexpr int kLutAndOr = (0xF0 & 0xCC) | 0xAA;  // (a & b) | c
+
+__device__ __forceinline__ void dequant_pair(uint32_t q, half2& lo, half2& hi) {
+  const uint32_t l = lop3<kLutAndOr>(q, 0x000f000fu, 0x64006400u);
+  const uint32_t h = lop3<kLutAndOr>(q, 0x00f000f0u, 0x64006400u);
+  const uint32_t kSub = 0x64086408u;  // (1032, 1032)
+  const uint32_t kMul = 0x2c002c00u;  // (1/16, 1/16)
+  const uint32_t kAdd = 0xd480d480u;  // (-72, -72)
+  lo = __hsub2(*reinterpret_cast<const half2*>(&l), *reinterpret_cast<const half2*>(&kSub));
+  hi = __hfma2(*reinterpret_cast<const half2*>(&h), *reinterpret_cast<const half2*>(&kMul),
+               *reinterpret_cast<const half2*>(&kAdd));
+}
+
+// ---------------------------------------------------------------------------
+// Sparse tensor-core MMA m16n8k32 (fp16 x fp16 -> fp32), 2:4 on operand A.
+// a: 4 regs of the compressed 16x16 A tile; b: 4 regs of the dense 32x8 B
+// tile; e: metadata register; SEL: sparsity selector (which thread pair of
+// each quad supplies metadata).
+// ---------------------------------------------------------------------------
+template <int SEL>
+__device__ __forceinline__ void mma_sp_16832(float (&c)[4], const uint32_t (&a)[4],
+                                             uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3,
+                                             uint32_t e) {
+  asm volatile(
+      "mma.sp::ordered_metadata.sync.aligned.m16n8k32.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9,%10,%11}, {%0,%1,%2,%3}, %12, %13;"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(b2), "r"(b3),
+        "r"(e), "n"(SEL));
+}
+
+// ---------------------------------------------------------------------------
+// 3-bit metadata decode.
+//
+// Eight 3-bit codes in bits [0,24) are spread to nibbles (code i in bits
+// [4i, 4i+3)), then every output bit is one lop3 over the three code bits
+// aligned to that position.  LUT byte bit v = output bit for code v; the two
+// tables are the codec's "high" map [E,D,8,D,3,4,9,C] and "low" map
+// [C,D,E,A,8,9,4,0] (codes 3/4 resp. 3/7 are never produced by the packer).
+// Bits [24,32) of the input are ignored.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t spread24(uint32_t x) {
+  constexpr int kSel = ((0xAA & 0xF0) | (~0xAA & 0xCC)) & 0xFF;  // c ? a : b (bitwise)
+  x = lop3<kSel>(x << 4, x, 0x0fff0000u);
+  x = lop3<kSel>(x << 2, x, 0x3f003f00u);
+  x = lop3<kSel>(x << 1, x, 0x70707070u);
+  return x;
+}
+
+template <int L0, int L1, int L2, int L3>
+__device__ __forceinline__ uint32_t decode_spread(uint32_t x) {
+  // lop3 argument order (a, b, c) = (code bit 2, code bit 1, code bit 0).
+  const uint32_t b0 = lop3<L0>(x >> 2, x >> 1, x) & 0x11111111u;
+  const uint32_t b1 = lop3<L1>(x >> 1, x, x << 1) & 0x22222222u;
+  const uint32_t b2 = lop3<L2>(x, x << 1, x << 2) & 0x44444444u;
+  const uint32_t b3 = lop3<L3>(x << 1, x << 2, x << 3) & 0x88888888u;
+  return (b0 | b1) | (b2 | b3);
+}
+
+__device__ __forceinline__ uint32_t decode24_high(uint32_t x) {
+  return decode_spread<0x5A, 0x11, 0xAB, 0xCF>(spread24(x));
+}
+
+__device__ __forceinline__ uint32_t decode24_low(uint32_t x) {
+  return decode_spread<0x22, 0x0C, 0x47, 0x3F>(spread24(x));
+}
+
+// Lane-pair decode: lanes 0..15 hold (X, Y) words of their 48-bit pair,
+// lanes 16..31 hold (Y, Z).  Produces the lane's two 4-bit metadata words
+// (original words `lane` and `32 + lane` of the 64-word block).
+__device__ __forceinline__ void meta3_pair_decode(uint32_t a, uint32_t b, bool upper,
+                                                  uint32_t& w0, uint32_t& w1) {
+  const uint32_t hi_in = upper ? __funnelshift_r(a, b, 16) : a;
+  const uint32_t lo_in = upper ? (b >> 8) : __funnelshift_r(a, b, 24);
+  w0 = decode24_high(hi_in);
+  w1 = decode24_low(lo_in);
+}
+
+}  // namespace sm100

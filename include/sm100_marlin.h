@@ -1,0 +1,124 @@
+/*
+ * C ABI of the sm_100a 2:4 sparse W4A16 GEMM library (libsm100_marlin.so).
+ *
+ * Drop-in for the CUDA entry points of hyeonu453/CSED499II's Sparse-Marlin
+ * path.  Plain pointers and sizes only; every function returns an int status
+ * (0 = success, see SM100_MARLIN_* below) and never throws.  Streams are
+ * passed as `void*` holding a cudaStream_t (NULL = legacy default stream).
+ *
+ * Naming: `prob_m` is the number of OUTPUT FEATURES (N), `prob_n` the number
+ * of BATCH ROWS (M) and `prob_k` the number of input features (K), exactly as
+ * the reference launcher names them.
+ */
+#ifndef SM100_MARLIN_H_
+#define SM100_MARLIN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  1 and 2 have the meaning of the reference's ERR_PROB_SHAPE /
+ * ERR_KERN_SHAPE (kernel_experiments/sparse_marlin/src/marlin/
+ * marlin_cuda_kernel_nm.cu:748-749). */
+#define SM100_MARLIN_OK 0
+#define SM100_MARLIN_ERR_PROB_SHAPE 1
+#define SM100_MARLIN_ERR_KERN_SHAPE 2
+#define SM100_MARLIN_ERR_CUDA 3
+#define SM100_MARLIN_ERR_ALIGNMENT 4
+#define SM100_MARLIN_ERR_ARGUMENT 5
+#define SM100_MARLIN_ERR_SCRATCH 6
+
+/* Bits of the device status word (sm100_marlin_device_status). */
+#define SM100_MARLIN_STATUS_FULL_WAIT_TIMEOUT 1
+#define SM100_MARLIN_STATUS_EMPTY_WAIT_TIMEOUT 2
+
+/*
+ * C[prob_n, prob_m] (fp16, row-major) = A[prob_n, prob_k] (fp16, row-major)
+ *     x dequant(B, meta, s)[prob_k, prob_m].
+ *
+ * Replaces `int marlin::marlin_cuda_2_4(const void*A, const void*B, const
+ * void*meta, void*C, void*s, int prob_m, int prob_n, int prob_k, void*
+ * workspace, int groupsize, int dev, cudaStream_t stream, int thread_k, int
+ * thread_m, int sms, int max_par)` (marlin_cuda_kernel_nm.cu:751-755, bound by
+ * marlin_cuda.cpp:25-29), with the same arguments and validation:
+ *   B          int32 (prob_k/32, 2*prob_m), Sparse-Marlin packed INT4 nonzeros
+ *   meta       int16 (prob_m, prob_k/16), reordered 2:4 metadata
+ *   s          fp16 (prob_k/128, prob_m) group scales, or (1, prob_m)
+ *   workspace  int32 array of >= prob_m/128*max_par entries, all zero on
+ *              entry; left all zero on exit
+ *   groupsize  compressed group size prob_k/2/s_rows (64 for 128-wide groups)
+ *              or -1 for one scale per column
+ *   thread_k, thread_m  -1 (auto) or one of the reference tiles (128,128)
+ *              for prob_n <= 16 and (64,256); they only select the reference's
+ *              shape checks, the B200 kernel picks its own tiling
+ *   sms        number of persistent CTAs (-1 = all SMs of `dev`)
+ * The call is asynchronous on `stream`.  Split-K scratch is taken from a
+ * per-(device, stream) cache owned by the library (allocated on first use; call
+ * once before any stream capture).  Concurrent calls on different streams
+ * need distinct workspaces, as in the reference.
+ */
+int sm100_marlin_mul_2_4(const void* A, const void* B, const void* meta, void* C, const void* s,
+                         int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
+                         int dev, void* stream, int thread_k, int thread_m, int sms, int max_par);
+
+/*
+ * Same GEMM with 3-bit metadata: `meta3` is int32 of prob_m*prob_k*3/128
+ * words produced by sm100_marlin_meta3_pack.  Replaces the reference's
+ * `metadata_decode.fetch` / `metadata_decode.matmul` variants
+ * (kernel_experiments/sparse_marlin/metadata_decode/setup.py:36-51), which
+ * accept the same arguments as mul_2_4.
+ */
+int sm100_marlin_mul_2_4_meta3(const void* A, const void* B, const void* meta3, void* C,
+                               const void* s, int prob_m, int prob_n, int prob_k, void* workspace,
+                               int groupsize, int dev, void* stream, int thread_k, int thread_m,
+                               int sms, int max_par);
+
+/* Split-K scratch bytes needed by a call with these sizes (for _ex). */
+size_t sm100_marlin_scratch_bytes(int prob_m, int prob_n, int prob_k, int dev, int sms);
+
+/* mul_2_4 / mul_2_4_meta3 with caller-provided split-K scratch (device memory,
+ * 16-byte aligned, >= sm100_marlin_scratch_bytes bytes, contents irrelevant).
+ * `meta_bits` is 4 or 3.  No counterpart in the reference: it exists for
+ * integrators that manage device memory themselves. */
+int sm100_marlin_mul_2_4_ex(const void* A, const void* B, const void* meta, void* C, const void* s,
+                            int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
+                            int dev, void* stream, int thread_k, int thread_m, int sms,
+                            int max_par, int meta_bits, void* scratch, size_t scratch_bytes);
+
+/*
+ * 3-bit metadata codec.  Replaces `pack_metadata` / `unpack_metadata`
+ * (kernel_experiments/sparse_marlin/metadata_decode/codec.cu:30-41).
+ * pack:   meta int16[n_int16] (n_int16 % 128 == 0) -> out int32[n_int16*3/8];
+ *         illegal 2:4 nibbles are counted into *err_count (device uint32,
+ *         caller zeroes it; the reference raises when it is nonzero).
+ * unpack: in int32[n_int32] (n_int32 % 48 == 0) -> out int16[n_int32*8/3].
+ */
+int sm100_marlin_meta3_pack(const void* meta, void* out, int64_t n_int16, void* err_count,
+                            void* stream);
+int sm100_marlin_meta3_unpack(const void* in, void* out, int64_t n_int32, void* stream);
+
+/* Applies the device 3-bit decoders to n words: out_high[i] = high-table
+ * decode of in[i] bits [0,24), out_low[i] = low-table decode.  Exposes the
+ * in-kernel decoders (kernel_experiments/sparse_marlin/decoder_dependency/
+ * pair.cuh:3-23, decoder.cuh:46-76) for known-answer tests. */
+int sm100_marlin_meta3_decode_words(const void* in, void* out_high, void* out_low, int64_t n,
+                                    void* stream);
+
+/* Reads and clears the device status word of `dev` (synchronises the
+ * device).  Nonzero bits mean a kernel gave up a bounded wait. */
+int sm100_marlin_device_status(int dev, int* status);
+
+/* Static description of a status code. */
+const char* sm100_marlin_error_string(int code);
+
+/* Message of the last CUDA error seen by this library on this thread. */
+const char* sm100_marlin_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SM100_MARLIN_H_ */

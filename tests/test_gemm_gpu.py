@@ -1,0 +1,170 @@
+"""GPU parity of the sm_100a 2:4 W4A16 GEMM against the CPU oracle.
+
+Cases follow the reference's own test matrix
+(``kernel_experiments/sparse_marlin/src/test_2_4.py:91-135``), extended to
+batch sizes where the reference kernel itself fails (48..256) and checked for
+run-to-run determinism.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import marlin24_oracle as O
+from conftest import GOLDEN, golden_cases
+from problems import (REL_FRO_TOL, REL_MAE_TOL, activations, errors, quantized_problem,
+                      random_packed_problem)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _setup():
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    import csed499ii_b200 as m
+
+    assert m.device_status(0) == 0
+
+
+def run(A, B, meta, s, N, thread_k=-1, thread_m=-1, sms=-1, max_par=16):
+    import csed499ii_b200 as m
+
+    A_d = torch.from_numpy(A).to(DEV)
+    C = torch.zeros((A.shape[0], N), dtype=torch.half, device=DEV)
+    ws = torch.zeros(N // 128 * max_par, dtype=torch.int32, device=DEV)
+    m.mul_2_4(A_d, torch.from_numpy(B).to(DEV), torch.from_numpy(meta).to(DEV), C,
+              torch.from_numpy(s).to(DEV), ws, thread_k, thread_m, sms, max_par)
+    torch.cuda.synchronize()
+    assert int(ws.abs().sum().item()) == 0, "workspace must be left zero"
+    return C
+
+
+def oracle_c(A, W):
+    return torch.from_numpy(A).to(DEV).float() @ torch.from_numpy(W).to(DEV).float()
+
+
+def check(C, C_ref):
+    rel_mae, rel_fro, _ = errors(C, C_ref)
+    assert torch.isfinite(C).all()
+    assert rel_mae < REL_MAE_TOL, rel_mae
+    assert rel_fro <= REL_FRO_TOL, rel_fro
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_golden_fixtures(name):
+    z = np.load(os.path.join(GOLDEN, name))
+    N = int(z["N"])
+    for rows in (1, 5, 16):
+        A = np.ascontiguousarray(z["A"][:rows])
+        C = run(A, z["B"], z["meta"], z["s"], N)
+        check(C, torch.from_numpy(z["C_ref"][:rows]).to(DEV))
+
+
+def test_correctness():
+    # test_2_4.py:91-93
+    for (N, M, K, tk, tm, g) in [(256, 16, 256, 128, 128, -1), (21504, 16, 4096, 64, 256, 128)]:
+        W, B, s, meta = quantized_problem(N, K, g, seed=0)
+        A = activations(M, K)
+        check(run(A, B, meta, s, N, tk, tm), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 7, 8, 9, 12, 16, 24, 32, 48, 64, 65, 96, 128, 192, 256])
+@pytest.mark.parametrize("g", [-1, 128])
+def test_batch_sweep(M, g):
+    # test_2_4.py:95-101 (tiles) plus the batches where the reference fails
+    N, K = 512, 1024
+    W, B, s, meta = quantized_problem(N, K, g, seed=2)
+    A = activations(M, K, seed=M)
+    check(run(A, B, meta, s, N), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("tk,tm", [(64, 256), (128, 128)])
+@pytest.mark.parametrize("M", [1, 8, 16])
+def test_explicit_tiles(tk, tm, M):
+    N, K = 512, 1024
+    W, B, s, meta = quantized_problem(N, K, -1, seed=3)
+    A = activations(M, K)
+    check(run(A, B, meta, s, N, tk, tm), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("K", [704, 768, 832])
+def test_k_stages_divisibility(K):
+    # test_2_4.py:103-106
+    W, B, s, meta = quantized_problem(512, K, -1, seed=4)
+    A = activations(16, K)
+    check(run(A, B, meta, s, 512, 64, 256), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("K", [64, 128, 192])
+def test_very_few_stages(K):
+    # test_2_4.py:108-111
+    W, B, s, meta = quantized_problem(768, K, -1, seed=5)
+    A = activations(16, K)
+    check(run(A, B, meta, s, 768, 64, 256), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("N,K", [(256, 512), (256, 1024), (256 * 128, 1024)])
+@pytest.mark.parametrize("tk,tm", [(128, 128), (64, 256)])
+def test_groups(N, K, tk, tm):
+    # test_2_4.py:129-135
+    W, B, s, meta = quantized_problem(N, K, 128, seed=6)
+    A = activations(16, K)
+    check(run(A, B, meta, s, N, tk, tm), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("N", [128, 384, 640])
+def test_column_tile_widths(N):
+    # N % 256 != 0 exercises the 128- and 64-column tile variants
+    K = 512
+    W, B, s, meta = quantized_problem(N, K, 128, seed=7)
+    A = activations(16, K)
+    check(run(A, B, meta, s, N), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("sms", [1, 3, 20, 77, 148, 300])
+def test_grid_sizes(sms):
+    W, B, s, meta = quantized_problem(1024, 2048, 128, seed=8)
+    A = activations(16, 2048)
+    check(run(A, B, meta, s, 1024, sms=sms), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("M", [16, 48, 64, 128])
+def test_deterministic_repeats(M):
+    # The reference kernel is nondeterministic at M >= 48
+    # (kernel_profile/SMOKE_K4096.md:7-23); this one must not be.
+    N, K = 4096, 4096
+    W, B, s, meta = random_packed_problem(N, K, 128, seed=9)
+    A = activations(M, K)
+    outs = [run(A, B, meta, s, N) for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    check(outs[0], oracle_c(A, W))
+
+
+LLAMA7B = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]
+
+
+@pytest.mark.parametrize("K,N", LLAMA7B)
+@pytest.mark.parametrize("M", [1, 16, 64])
+def test_llama7b_shapes(K, N, M):
+    W, B, s, meta = random_packed_problem(N, K, 128, seed=10)
+    A = activations(M, K)
+    check(run(A, B, meta, s, N), oracle_c(A, W))
+
+
+def test_reference_error_messages():
+    import csed499ii_b200 as m
+
+    A = torch.zeros((32, 256), dtype=torch.half, device=DEV)
+    C = torch.zeros((32, 384), dtype=torch.half, device=DEV)
+    B = torch.zeros((8, 768), dtype=torch.int32, device=DEV)
+    meta = torch.zeros((384, 16), dtype=torch.int16, device=DEV)
+    s = torch.zeros((1, 384), dtype=torch.half, device=DEV)
+    ws = torch.zeros(48, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match=r"Problem \(m=384, n=32, k=256\) not compatible"):
+        m.mul_2_4(A, B, meta, C, s, ws)
+    with pytest.raises(RuntimeError, match="No kernel implementation for thread_k=128"):
+        m.mul_2_4(A, B, meta, C[:, :256].contiguous(), s[:, :256].contiguous(), ws, 128, 128)

@@ -1,0 +1,110 @@
+"""GPU parity of the 3-bit metadata codec and the 3-bit-metadata GEMM.
+
+Pack/unpack must be bit-exact against the oracle restatement of
+``metadata_decode/codec.cu``; the device decoders are checked exhaustively
+over all 2^24 code words against the reference's truth tables
+(``decoder_dependency/pair.cu:11-30``); the 3-bit GEMM must equal the 4-bit
+GEMM bit for bit (same arithmetic, only the metadata encoding differs) --
+the reference's own pass rule (``metadata_decode/smoke.py:17-39``).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import marlin24_oracle as O
+from conftest import GOLDEN, golden_cases
+from problems import REL_FRO_TOL, REL_MAE_TOL, activations, errors, quantized_problem, random_packed_problem
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def test_pack_unpack_bit_exact_on_reference_metadata():
+    from csed499ii_b200 import metadata_decode as md
+
+    for name in golden_cases():
+        meta = np.load(os.path.join(GOLDEN, name))["meta"]
+        packed = md.pack(torch.from_numpy(meta).to(DEV))
+        ref, err = O.meta3_pack(meta)
+        assert err == 0
+        assert np.array_equal(packed.cpu().numpy(), ref)
+        restored = md.unpack(packed)
+        assert torch.equal(restored.cpu(), torch.from_numpy(meta.reshape(-1)))
+
+
+def test_pack_rejects_illegal_nibbles():
+    from csed499ii_b200 import metadata_decode as md
+
+    meta = torch.full((256,), 0x4444, dtype=torch.int16, device=DEV)
+    meta[3] = 0x4F44
+    with pytest.raises(RuntimeError, match="unsupported 2:4 nibbles"):
+        md.pack(meta)
+    with pytest.raises(RuntimeError, match="multiple of 256 bytes"):
+        md.pack(meta[:100])
+    with pytest.raises(RuntimeError, match="expected compressed metadata"):
+        md.unpack(torch.zeros(47, dtype=torch.int32, device=DEV))
+
+
+def test_decoders_exhaustive():
+    from csed499ii_b200 import metadata_decode as md
+
+    x = np.arange(1 << 24, dtype=np.uint32)
+    garbage = ((x * np.uint32(1664525) + np.uint32(1013904223)) & np.uint32(0xFF)) << np.uint32(24)
+    xin = torch.from_numpy((x | garbage).view(np.int32)).to(DEV)
+    hi, lo = md.decode_words(xin)
+    assert np.array_equal(hi.cpu().numpy().view(np.uint32), O.decode24(x, O.DEC_HIGH))
+    assert np.array_equal(lo.cpu().numpy().view(np.uint32), O.decode24(x, O.DEC_LOW))
+
+
+def _gemm(A, B, meta, s, N, meta3):
+    import csed499ii_b200 as m
+    from csed499ii_b200 import metadata_decode as md
+
+    A_d = torch.from_numpy(A).to(DEV)
+    C = torch.zeros((A.shape[0], N), dtype=torch.half, device=DEV)
+    ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=DEV)
+    B_d, s_d = torch.from_numpy(B).to(DEV), torch.from_numpy(s).to(DEV)
+    meta_d = torch.from_numpy(meta).to(DEV)
+    if meta3:
+        md.matmul(A_d, B_d, md.pack(meta_d), C, s_d, ws)
+    else:
+        m.mul_2_4(A_d, B_d, meta_d, C, s_d, ws)
+    torch.cuda.synchronize()
+    return C
+
+
+@pytest.mark.parametrize("M", [1, 16, 64])
+def test_meta3_gemm_equals_meta4_gemm(M):
+    W, B, s, meta = quantized_problem(4096, 4096, 128, seed=20261019)
+    A = activations(M, 4096)
+    c4 = _gemm(A, B, meta, s, 4096, False)
+    c3 = _gemm(A, B, meta, s, 4096, True)
+    assert torch.equal(c3, c4)
+    rel_mae, rel_fro, _ = errors(c3, torch.from_numpy(A).to(DEV).float() @ torch.from_numpy(W).to(DEV).float())
+    assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL
+
+
+@pytest.mark.parametrize("K,N", [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)])
+@pytest.mark.parametrize("M", [1, 16, 64])
+def test_meta3_llama7b_shapes(K, N, M):
+    W, B, s, meta = random_packed_problem(N, K, 128, seed=11)
+    A = activations(M, K)
+    c3 = _gemm(A, B, meta, s, N, True)
+    c4 = _gemm(A, B, meta, s, N, False)
+    assert torch.equal(c3, c4)
+    rel_mae, rel_fro, _ = errors(c3, torch.from_numpy(A).to(DEV).float() @ torch.from_numpy(W).to(DEV).float())
+    assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL
+
+
+def test_meta3_shape_checks():
+    from csed499ii_b200 import metadata_decode as md
+
+    a = torch.zeros((1, 256), dtype=torch.half, device=DEV)
+    c = torch.zeros((1, 256), dtype=torch.half, device=DEV)
+    bad = torch.zeros(10, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="unsupported compressed metadata shape"):
+        md.fetch(a, None, bad, c, None, None)
+    with pytest.raises(RuntimeError, match="a must be contiguous CUDA half"):
+        md.fetch(a.float(), None, bad, c, None, None)
