@@ -1,0 +1,392 @@
+"""Benchmark of the sm_100a 2:4 sparse W4A16 GEMM (driver contract).
+
+Workload (Llama-2-7B decode): one *step* is one decode
+step of all 32 transformer layers' four projection GEMMs --
+(K, N) in {(4096, 12288) qkv, (4096, 4096) o, (4096, 22016) gate+up,
+(11008, 4096) down} -- at M = 16 batch rows, 2:4 INT4 weights with group-128
+fp16 scales and 4-bit 2:4 metadata (``--meta-bits 3`` for the 3-bit variant).
+Every layer has its own weights (2.4 GB per GPU, far above the 126 MB L2), so
+each step streams its weights from HBM.  The 128 launches of a step are
+captured in a CUDA graph and replayed.
+
+Lines printed (rank 0, one JSON line):
+* ``value``  -- algorithmic bytes (bench.py:170 of the reference: A + B + meta
+  + s + C) of all ranks / max-over-ranks device time, GB/s, inputs resident.
+* ``e2e``    -- same metric through the public Python operator
+  (``csed499ii_b200.mul_2_4``), eager launches, with the step's activations
+  copied from pinned host memory and the last layer's outputs copied back
+  inside the timed region.
+* ``roofline`` -- GEMM kernel achieved GB/s vs the measured HBM copy peak.
+* ``cpu_baseline`` -- the CPU oracle (numpy dequantise-then-matmul, the
+  reference's torch fp32 oracle path) on a bounded sample.
+
+``--impl reference`` times the reference's CPU path (the oracle port) alone.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS = 32
+SHAPES = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]  # (K, N)
+GROUP = 128
+
+
+def algo_bytes(M, K, N, meta_bits):
+    meta = K * N // 8 if meta_bits == 4 else 3 * K * N // 32
+    return K * N // 4 + meta + 2 * N * K // GROUP + 2 * M * K + 2 * M * N
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML)
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [k for k, v in self.REASONS.items() if self.reasons & v and k != "gpu_idle"]
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------
+# synthetic weights (random packed operator inputs; timing is data-independent)
+# ----------------------------------------------------------------------------
+def make_layer(torch, K, N, dev, gen, meta_bits):
+    legal = torch.tensor([0x4, 0x8, 0x9, 0xC, 0xD, 0xE], dtype=torch.int32, device=dev)
+    B = torch.randint(-(2**31), 2**31 - 1, (K // 32, 2 * N), dtype=torch.int32, device=dev, generator=gen)
+    idx = torch.randint(0, 6, (N * K // 16, 4), device=dev, generator=gen)
+    nib = legal[idx]
+    meta = (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).to(torch.int16)
+    meta = meta.view(N, K // 16).contiguous()
+    s = (torch.rand((K // GROUP, N), device=dev, generator=gen) * 0.02 + 0.01).half() * (2 / 15)
+    if meta_bits == 3:
+        from csed499ii_b200 import metadata_decode as md
+
+        meta = md.pack(meta)
+    return B, meta, s.contiguous()
+
+
+def bench_ours(args, torch, dist, rank, world, dev):
+    import csed499ii_b200 as m
+    from csed499ii_b200 import metadata_decode as md
+
+    lib = m._ext.load()
+    M = args.m
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    layers = [[make_layer(torch, K, N, dev, gen, args.meta_bits) for (K, N) in SHAPES]
+              for _ in range(LAYERS)]
+    A = {K: torch.randn((M, K), dtype=torch.half, device=dev, generator=gen) for K in (4096, 11008)}
+    C = {N: torch.empty((M, N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
+    ws = torch.zeros(22016 // 128 * 16, dtype=torch.int32, device=dev)
+    devi = dev.index
+    fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
+    stream = torch.cuda.Stream(device=dev)
+
+    def step_raw(s_ptr):
+        for lay in layers:
+            for (K, N), (B, meta, s) in zip(SHAPES, lay):
+                rc = fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(), s.data_ptr(),
+                        N, M, K, ws.data_ptr(), GROUP // 2, devi, s_ptr, -1, -1, -1, 16)
+                if rc != 0:
+                    raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
+
+    bytes_step = LAYERS * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
+    launches_step = LAYERS * len(SHAPES) * ((M + 63) // 64)
+
+    # warm-up eagerly (sizes the split-K scratch before capture), then capture
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step_raw(stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_raw(torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize(dev)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(devi) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_step = ms / args.steps
+    value = bytes_step * world * args.steps / (ms * 1e-3) / 1e9
+    per_launch_us = ms * 1e3 / (args.steps * launches_step)
+    status = m.device_status(devi)
+    if status != 0:
+        raise RuntimeError(f"device status {status}: a bounded wait timed out")
+
+    # ---- per-shape kernel times (for the detail block), inputs resident
+    detail = {}
+    for (K, N), idx in zip(SHAPES, range(4)):
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            sp = torch.cuda.current_stream(dev).cuda_stream
+            for lay in layers:
+                B, meta, s = lay[idx]
+                fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(), s.data_ptr(),
+                   N, M, K, ws.data_ptr(), GROUP // 2, devi, sp, -1, -1, -1, 16)
+        for _ in range(3):
+            g2.replay()
+        torch.cuda.synchronize(dev)
+        reps = max(3, min(50, args.steps))
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                g2.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        us = ev0.elapsed_time(ev1) * 1e3 / (reps * LAYERS)
+        b = algo_bytes(M, K, N, args.meta_bits)
+        detail[f"{K}x{N}"] = {"us": round(us, 3), "GB/s": round(b / us / 1e3, 1),
+                              "TFLOP/s": round(2 * M * K * N / us / 1e6, 2)}
+        del g2
+
+    # ---- end to end through the public operator, host buffers
+    A_h = {K: A[K].cpu().pin_memory() for K in A}
+    C_h = {N: torch.empty((M, N), dtype=torch.half).pin_memory() for N in C}
+    A_d = {K: torch.empty_like(A[K]) for K in A}
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for K in A_h:
+            A_d[K].copy_(A_h[K], non_blocking=True)
+        for lay in layers:
+            for (K, N), (B, meta, s) in zip(SHAPES, lay):
+                if args.meta_bits == 4:
+                    m.mul_2_4(A_d[K], B, meta, C[N], s, ws)
+                else:
+                    md.matmul(A_d[K], B, meta, C[N], s, ws)
+        for N in C_h:
+            C_h[N].copy_(C[N], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = bytes_step * world * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    h2d = sum(t.numel() * 2 for t in A_h.values())
+    d2h = sum(t.numel() * 2 for t in C_h.values())
+
+    peak, peak_kind = load_peaks()
+    achieved = bytes_step / LAYERS / len(SHAPES) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
+    return dict(
+        value=value, ms_step=ms_step, per_launch_us=per_launch_us, bytes_step=bytes_step,
+        launches=launches_step * args.steps, clocks=clk.summary(), detail=detail,
+        e2e=dict(value=round(e2e_value, 2), unit="GB/s", h2d_bytes_per_step=h2d,
+                 d2h_bytes_per_step=d2h, steps=e2e_steps,
+                 ms_per_step=round(e2e_ms / e2e_steps, 4)),
+        roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s",
+                      frac=round(achieved / peak, 4), traffic=None,
+                      peak_source=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"),
+    )
+
+
+# ----------------------------------------------------------------------------
+# CPU oracle (the reference's dequantise-then-matmul path)
+# ----------------------------------------------------------------------------
+def cpu_reference(M, meta_bits, reps, layers_sample=1, budget_s=25.0):
+    """Time the CPU oracle on one layer's four GEMMs (bounded sample)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import marlin24_oracle as O
+
+    rng = np.random.default_rng(0)
+    Ws, As = [], {}
+    for (K, N) in SHAPES:
+        B = rng.integers(0, 2**32, size=(K // 32, 2 * N), dtype=np.uint64).astype(np.uint32).view(np.int32)
+        nib = rng.choice(np.array([0x4, 0x8, 0x9, 0xC, 0xD, 0xE], dtype=np.uint16), size=(N * K // 16, 4))
+        meta = (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).astype(np.uint16)
+        meta = meta.view(np.int16).reshape(N, K // 16)
+        s = (rng.uniform(0.01, 0.03, size=(K // GROUP, N)) * 2 / 15).astype(np.float16)
+        Ws.append(O.dequant_2_4(B, meta, s, K, N, GROUP).astype(np.float32))
+        As.setdefault(K, rng.standard_normal((M, K)).astype(np.float16).astype(np.float32))
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    bytes_layer = sum(algo_bytes(M, K, N, meta_bits) for (K, N) in SHAPES)
+    times = []
+    t_start = time.perf_counter()
+    for r in range(reps):
+        t0 = time.perf_counter()
+        for (K, N), W in zip(SHAPES, Ws):
+            _ = As[K] @ W
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    t = statistics.median(times)
+    return dict(value=round(bytes_layer / t / 1e9, 3), unit="GB/s", cores=cores, kind="port",
+                sample=(f"one Llama-2-7B layer (4 GEMMs, M={M}) of the 32-layer step; numpy fp32 "
+                        f"A @ dequant(W) with W dequantised once by the oracle; median of {len(times)} reps"),
+                seconds_per_layer=t)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--m", type=int, default=16)
+    ap.add_argument("--meta-bits", type=int, choices=[3, 4], default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    config = {"workload": f"Llama-2-7B decode step: 32 layers x 4 GEMMs "
+                          f"(K,N) in {SHAPES}, M={args.m}, 2:4 INT4 g128, {args.meta_bits}-bit meta",
+              "model_shapes": "Llama-2-7B", "batch_rows": args.m, "groupsize": GROUP,
+              "meta_bits": args.meta_bits, "layers": LAYERS,
+              "l2": "inputs larger than L2: 32 distinct layers' weights (2.4 GB) per step",
+              "parallelism": f"replicas x{args.gpus} (independent layers per GPU)"}
+    metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-7B decode layer set, M={args.m})"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ref = cpu_reference(args.m, args.meta_bits, reps=max(args.steps, 1))
+        line = dict(metric=metric, value=ref["value"], unit="GB/s", n_gpus=args.gpus,
+                    steps=args.steps, warmup=args.warmup, ms_per_step=round(ref["seconds_per_layer"] * LAYERS * 1e3, 3),
+                    higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
+                    data="synthetic", config=config, impl="reference",
+                    cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    e2e={"value": ref["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dev = torch.device("cuda", local)
+    else:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+
+    res = bench_ours(args, torch, dist, rank, world, dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = cpu_reference(args.m, args.meta_bits, reps=10)
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        line = dict(metric=metric, value=round(res["value"], 2), unit="GB/s", n_gpus=world,
+                    steps=args.steps, warmup=args.warmup, ms_per_step=round(res["ms_step"], 5),
+                    higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f16",
+                    data="synthetic (random packed INT4 codes, random legal 2:4 metadata, "
+                         "random fp16 group scales; seeded)",
+                    config=config, e2e=res["e2e"], roofline=res["roofline"],
+                    cpu_baseline=cpu, clocks=res["clocks"], gpu_launches=res["launches"],
+                    per_launch_us=round(res["per_launch_us"], 3), detail=res["detail"])
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
