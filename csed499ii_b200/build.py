@@ -51,13 +51,18 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in _sources())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
-    """Compile the library if any source is newer than it; return its path."""
-    if not force and not ptxas_info and up_to_date():
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False,
+          out: str = LIB_PATH, defines=()) -> str:
+    """Compile the library if any source is newer than it; return its path.
+
+    ``defines`` (e.g. ``["SM100_MARLIN_TRACE=1"]``) build a variant into
+    ``out``; the default build has none.
+    """
+    if not force and not ptxas_info and not defines and out == LIB_PATH and up_to_date():
         return LIB_PATH
-    os.makedirs(LIB_DIR, exist_ok=True)
-    tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS]
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    tmp = out + ".tmp"
+    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS] + [f"-D{d}" for d in defines]
     if ptxas_info:
         cmd += ["-Xptxas", "-v"]
     cmd += ["-cudart", "static", "-o", tmp, os.path.join(CSRC, "sm100_marlin.cu")]
@@ -68,8 +73,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
     if verbose or ptxas_info:
         sys.stdout.write(res.stdout + res.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":

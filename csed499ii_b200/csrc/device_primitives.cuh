@@ -75,18 +75,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Wait for the phase of `parity` to complete.  Returns false (and leaves the
 // wait) when `*abort` is raised by another thread of the CTA or when the wait
 // exceeds kWaitLimitNs; in the latter case it raises `*abort` itself.
+// %globaltimer is slow to read, so the abort flag and the clock are only
+// checked every 1024 unsuccessful polls: a normal wait never touches them.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_timer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0 = 0;
+  uint32_t polls = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++polls & 1023u) != 0) continue;
     if (*abort) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
       *abort = 1;
       return false;
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -112,6 +118,32 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// 2-D tiled TMA load global -> shared (no multicast), completing on an
+// mbarrier.  (x, y) are element coordinates of the box origin; x times the
+// element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// 3-D tiled TMA load (no multicast); x is the innermost coordinate.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -9,25 +9,31 @@
 // kernel_experiments/sparse_marlin/metadata_decode/codec.cu:18-24).
 //
 // Design (B200-first, not a translation of marlin_cuda_kernel_nm.cu):
-//  * Work = column tiles of 64*NC out-features x K.  The (tile, kk) "units"
-//    (kk = 32 dense K) are laid out tile-major and split evenly over a
-//    persistent grid of one CTA per SM, so every SM streams the same number
-//    of weight bytes whatever the shape (stream-K style split).
-//  * One producer warp streams B rows, metadata rows, scale rows and the
-//    activation slice of each stage with cp.async.bulk into a deep
-//    shared-memory ring (mbarrier full/empty pairs, evict-first L2 policy for
-//    the weight stream).  Every wait is bounded (%globaltimer) and records a
-//    status bit instead of hanging.
-//  * Eight consumer warps each own one (kk, 64-column chunk) block per stage:
-//    one 16-byte B load, the metadata words (ldmatrix.x2 for 4-bit, two
-//    32-bit loads + lop3 decode for 3-bit), INT4 -> fp16 magic-number dequant
-//    with the group scale fused, and mma.sp m16n8k32 with fp32 accumulators.
+//  * Work = column tiles of 64*NC out-features x K.  The (tile, K-slice)
+//    "units" are laid out tile-major and split evenly over a persistent grid
+//    of one CTA per SM, so every SM streams the same number of weight bytes
+//    whatever the shape (stream-K style split).
+//  * Producer warps stream each stage -- SK rows of 32 dense K of B,
+//    metadata and scales of the tile, plus the activation slice -- with one
+//    TMA tensor copy per operand into a deep shared-memory ring (mbarrier
+//    full/empty pairs, evict-first L2 policy for the weight stream; the
+//    activation box is 128-byte swizzled so ldmatrix is bank-conflict free).
+//    A warp can only keep about one stage per ~0.3 us in flight on B200, so
+//    kProducerWarps warps take the stages round-robin.  Every wait is bounded
+//    (%globaltimer) and records a status bit instead of hanging.
+//  * Eight consumer warps each own one (32-K row, 64-column chunk) block per
+//    stage: one 16-byte B load, the metadata words (ldmatrix.x2 for 4-bit,
+//    two 32-bit loads + lop3 decode for 3-bit), INT4 -> fp16 magic-number
+//    dequant with the group scale fused, and mma.sp m16n8k32 with fp32
+//    accumulators.
 //  * Split-K partials are reduced in fp32: warps of a CTA through shared
 //    memory, CTAs of a tile through a scratch buffer and a per-tile ticket in
 //    the caller's workspace; the last CTA to arrive sums all partials in CTA
-//    order (deterministic, no CTA ever waits for another) and writes C.
+//    order with all its threads (deterministic; no CTA ever waits for another)
+//    and writes C.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -36,10 +42,11 @@
 namespace sm100 {
 
 struct GemmParams {
-  const uint8_t* A;     // fp16 (M, K) row-major, this launch's rows
-  const uint8_t* B;     // int32 (K/32, 2N)
-  const uint8_t* meta;  // K/32 rows of 4N bytes (4-bit) or 3N bytes (3-bit)
-  const uint8_t* s;     // fp16 (K/128, N) permuted, or (1, N)
+  CUtensorMap tm_a;     // A  fp16 (64, M rows, K/64) box (64, 16*MB, SK/2), 128B swizzle
+  CUtensorMap tm_b;     // B  u64  (K/32 rows, N)     box (64*NC, SK)
+  CUtensorMap tm_meta;  // meta u64 (K/32 rows, N/2 or 3N/8) box (32*NC or 24*NC, SK)
+  CUtensorMap tm_s;     // s  u64  (K/128 rows, N/4)  box (16*NC, S_ROWS)   (grouped only)
+  const uint8_t* s;     // fp16 scales (per-column epilogue reads)
   half* C;              // fp16 (M, N) row-major
   float4* partials;     // split-K scratch
   int* counters;        // one int per column tile; zero on entry and on exit
@@ -48,73 +55,143 @@ struct GemmParams {
   int N;
   int K;
   int grouped;          // 1: group of 128 dense K; 0: one scale per column
-  int n_tiles;          // N / (64*NC)
   int kk_total;         // K / 32
-  long long units;      // n_tiles * kk_total / 2   (a unit = 2 kk rows)
+  int unit_kk;          // 32-K rows per unit (2, 4 or 8); divides kk_total
+  long long units;      // n_tiles * kk_total / unit_kk
+  unsigned long long* trace;  // optional per-CTA timestamps (SM100_MARLIN_TRACE builds)
 };
 
+// Per-CTA timeline written when the library is built with
+// -DSM100_MARLIN_TRACE=1 (off by default): %globaltimer at kernel entry, first
+// TMA issue, first stage consumed, last stage consumed, end of epilogue, and
+// the number of stages and fixups of the CTA.
+constexpr int kTraceWords = 8;
+// CTA 0 additionally records per-stage times after the per-CTA words:
+// [stage][0] producer issue, [1..3] consumer warp 0 wait start / data ready /
+// done, [4..6] the same for the last consumer warp.
+constexpr int kTraceStages = 64;
+constexpr int kTraceStageWords = 8;
+#ifndef SM100_MARLIN_TRACE
+#define SM100_MARLIN_TRACE 0
+#endif
+
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarps = 4;
+// Consecutive 32-K rows of one chunk per consumer warp per stage: 2, except
+// for narrow tiles with many batch rows (64 columns above 16 rows, 128 columns
+// at 64 rows), whose activation slices would not fit a useful ring.
+constexpr int rows_per_warp(int nc, int mb) {
+  return ((nc == 1 && mb > 1) || (nc == 2 && mb == 4)) ? 1 : 2;
+}
+constexpr int kThreads = (kConsumerWarps + kProducerWarps) * 32;
 constexpr int kSmemBudget = 200 * 1024;
 
 template <int NC, int MB, bool META3>
 struct DecodeCfg {
-  static constexpr int SK = kConsumerWarps / NC;                 // kk rows per stage
-  static constexpr int B_ROW = 512 * NC;                         // bytes of B per kk row
-  static constexpr int M_BLK = META3 ? 192 : 256;                // meta bytes per (kk, chunk)
+  static constexpr int RPW = rows_per_warp(NC, MB);
+  static constexpr int SK = kConsumerWarps * RPW / NC;           // 32-K rows per stage
+  static constexpr int B_ROW = 512 * NC;                         // bytes of B per row
+  static constexpr int M_BLK = META3 ? 192 : 256;                // meta bytes per (row, chunk)
   static constexpr int M_ROW = M_BLK * NC;
   static constexpr int S_ROW = 128 * NC;                         // scale bytes per group row
-  static constexpr int S_ROWS = SK == 2 ? 1 : (SK == 4 ? 2 : 3); // groups a stage can touch
-  static constexpr int A_STRIDE = SK * 64 + 16;                  // padded activation row
-  static constexpr int OFF_B = 0;
+  static constexpr int S_ROWS = SK / 4;                          // group rows per stage
+  static constexpr int A_BOXES = SK / 2;                         // 64-K activation boxes
+  static constexpr int A_BOX = 16 * MB * 128;                    // bytes per activation box
+  static constexpr int OFF_A = 0;                                // 1024-aligned (swizzle atom)
+  static constexpr int OFF_B = OFF_A + A_BOXES * A_BOX;
   static constexpr int OFF_M = OFF_B + SK * B_ROW;
   static constexpr int OFF_S = OFF_M + SK * M_ROW;
-  static constexpr int OFF_A = OFF_S + S_ROWS * S_ROW;
-  static constexpr int STAGE_RAW = OFF_A + 16 * MB * A_STRIDE;
-  static constexpr int STAGE = (STAGE_RAW + 127) / 128 * 128;
+  static constexpr int STAGE_RAW = OFF_S + S_ROWS * S_ROW;
+  static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int ACC_F4 = 8 * MB;                          // float4 per thread of acc
   static constexpr int RED_BYTES = NC * ACC_F4 * 32 * 16;        // one slot per chunk
   static constexpr int HEADER = 1024;                            // barriers + flags
-  static constexpr int DEPTH_FIT = (kSmemBudget - HEADER - RED_BYTES) / STAGE;
-  static constexpr int DEPTH = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
-  static constexpr int SMEM = HEADER + RED_BYTES + DEPTH * STAGE;
+  static constexpr int RING_OFF = (HEADER + RED_BYTES + 1023) / 1024 * 1024;
+  static constexpr int DEPTH_FIT = (kSmemBudget - RING_OFF - 1024) / STAGE;
+  static constexpr int DEPTH_RAW = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
+  static constexpr int DEPTH = DEPTH_RAW / kProducerWarps * kProducerWarps;  // slots per producer equal
+  static constexpr int SMEM = RING_OFF + DEPTH * STAGE + 1024;   // +1024: base alignment slack
+  static constexpr uint32_t STAGE_TX_NOSCALE = A_BOXES * A_BOX + SK * (B_ROW + M_ROW);
+  static_assert(DEPTH >= kProducerWarps, "ring too shallow for the producer warps");
+  static constexpr uint32_t STAGE_TX_SCALE = STAGE_TX_NOSCALE + S_ROWS * S_ROW;
+  static constexpr int FIX_F4 = NC * ACC_F4;                     // float4 per thread in the fixup
   static_assert(DEPTH >= 4, "ring too shallow");
+  static_assert(SK % 4 == 0, "stage must hold whole scale groups");
 };
 
+// floor(num / den) for 0 <= num < 2^53, den > 0, without the slow 64-bit
+// integer division: a double quotient corrected by at most one step.
+__device__ __forceinline__ long long floor_div(long long num, long long den) {
+  long long q = static_cast<long long>(static_cast<double>(num) / static_cast<double>(den));
+  if (q * den > num) --q;
+  if ((q + 1) * den <= num) ++q;
+  return q;
+}
 // Unit range of CTA c in a split of `units` over `grid` CTAs.
 __device__ __forceinline__ long long unit_begin(long long c, long long units, long long grid) {
-  return (c * units) / grid;
+  return floor_div(c * units, grid);
 }
 // CTA owning unit u (the largest c with unit_begin(c) <= u).
 __device__ __forceinline__ long long unit_owner(long long u, long long units, long long grid) {
-  return ((u + 1) * grid - 1) / units;
+  return floor_div((u + 1) * grid - 1, units);
 }
 
-template <int NC, int MB, int NH_LAST, bool META3>
-__global__ void __maxnreg__(224)
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Element i (0..3) of float4 v of lane `lane` of a chunk's accumulator slot:
+// v = (mb*4 + j)*2 + h, element e -> (out-feature in chunk, batch row).
+__device__ __forceinline__ void acc_coords(int v, int lane, int e, int& n_in_chunk, int& row) {
+  const int h = v & 1;
+  const int j = (v >> 1) & 3;
+  const int mb = v >> 3;
+  const int g = lane >> 2, t = lane & 3;
+  n_in_chunk = 8 * g + j + 4 * (e >> 1);
+  row = 16 * mb + 8 * h + 2 * t + (e & 1);
+}
+
+template <int NC, int MB, int NH_LAST, bool META3, bool GROUPED>
+__global__ void __launch_bounds__(kThreads, 1)
     marlin24_decode_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = DecodeCfg<NC, MB, META3>;
   constexpr int SK = Cfg::SK;
   constexpr int D = Cfg::DEPTH;
 
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment of the ring (128B-swizzle atoms).
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty_bar = full_bar + D;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 512);
   volatile int* ticket_sh = reinterpret_cast<volatile int*>(smem + 516);
   uint8_t* red = smem + Cfg::HEADER;
-  uint8_t* ring = red + Cfg::RED_BYTES;
+  uint8_t* ring = smem + Cfg::RING_OFF;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  unsigned long long* trace =
+      SM100_MARLIN_TRACE && p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceWords : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = global_timer_ns();
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < D; ++i) {
-      mbar_init(smem_addr(&full_bar[i]), 1);
-      mbar_init(smem_addr(&empty_bar[i]), kConsumerWarps);
-    }
-    *abort_flag = 0;
+  if (threadIdx.x < D) {
+    mbar_init(smem_addr(&full_bar[threadIdx.x]), 1);
+    mbar_init(smem_addr(&empty_bar[threadIdx.x]), kConsumerWarps);
     fence_mbar_init();
+  }
+  if (threadIdx.x == 0) *abort_flag = 0;
+  if (threadIdx.x == kConsumerWarps * 32) {
+    prefetch_tmap(&p.tm_a);
+    prefetch_tmap(&p.tm_b);
+    prefetch_tmap(&p.tm_meta);
+    if (GROUPED) prefetch_tmap(&p.tm_s);
   }
   __syncthreads();
 
@@ -122,61 +199,49 @@ __global__ void __maxnreg__(224)
   const long long cta = blockIdx.x;
   const long long u_begin = unit_begin(cta, p.units, grid);
   const long long u_end = unit_begin(cta + 1, p.units, grid);
-  const int units_per_tile = p.kk_total >> 1;
+  const int units_per_tile = p.kk_total / p.unit_kk;
+  const int ukk = p.unit_kk;
   const uint32_t ring_base = smem_addr(ring);
 
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------------ producer
-    const uint64_t pol_stream = policy_evict_first();
-    const uint64_t pol_keep = policy_evict_last();
-    const long long b_row_stride = 8ll * p.N;                     // bytes per kk row of B
-    const long long m_row_stride = (META3 ? 3ll : 4ll) * p.N;      // bytes per kk row of meta
-    const long long s_row_stride = 2ll * p.N;
-    const long long a_row_stride = 2ll * p.K;
-    uint32_t stage = 0;
-    bool ok = true;
-    for (long long u = u_begin; u < u_end && ok;) {
-      const int tile = static_cast<int>(u / units_per_tile);
-      const int ub = static_cast<int>(u % units_per_tile);
-      const long long ue_ll = ub + (u_end - u);
-      const int ue = ue_ll < units_per_tile ? static_cast<int>(ue_ll) : units_per_tile;
-      u += ue - ub;
-      const int kb = 2 * ub, ke = 2 * ue;
-      for (int kk0 = kb; kk0 < ke; kk0 += SK, ++stage) {
-        const int rows = min(SK, ke - kk0);
-        const int slot = stage % D;
-        const uint32_t parity = ((stage / D) & 1u) ^ 1u;
-        if (!mbar_wait_bounded(smem_addr(&empty_bar[slot]), parity, abort_flag)) {
-          if (lane == 0) atomicOr(p.status, kStatusEmptyWaitTimeout);
-          ok = false;
-          break;
-        }
-        const int g_lo = kk0 >> 2, g_hi = (kk0 + rows - 1) >> 2;
-        const int n_srows = p.grouped ? (g_hi - g_lo + 1) : 0;
-        const uint32_t bytes = rows * (Cfg::B_ROW + Cfg::M_ROW) + n_srows * Cfg::S_ROW +
-                               p.M * rows * 64;
-        const uint32_t full = smem_addr(&full_bar[slot]);
-        if (lane == 0) mbar_arrive_expect_tx(full, bytes);
-        __syncwarp();
-        const uint32_t st = ring_base + slot * Cfg::STAGE;
-        const long long col_b = static_cast<long long>(tile) * Cfg::B_ROW;
-        const long long col_m = static_cast<long long>(tile) * Cfg::M_ROW;
-        if (lane < rows) {
-          bulk_g2s(st + Cfg::OFF_B + lane * Cfg::B_ROW,
-                   p.B + (kk0 + lane) * b_row_stride + col_b, Cfg::B_ROW, full, pol_stream);
-        } else if (lane >= 8 && lane < 8 + rows) {
-          const int r = lane - 8;
-          bulk_g2s(st + Cfg::OFF_M + r * Cfg::M_ROW, p.meta + (kk0 + r) * m_row_stride + col_m,
-                   Cfg::M_ROW, full, pol_stream);
-        } else if (lane >= 16 && lane < 16 + n_srows) {
-          const int r = lane - 16;
-          bulk_g2s(st + Cfg::OFF_S + r * Cfg::S_ROW,
-                   p.s + (g_lo + r) * s_row_stride + static_cast<long long>(tile) * Cfg::S_ROW,
-                   Cfg::S_ROW, full, pol_keep);
-        }
-        for (int m = lane; m < p.M; m += 32) {
-          bulk_g2s(st + Cfg::OFF_A + m * Cfg::A_STRIDE, p.A + m * a_row_stride + kk0 * 64,
-                   rows * 64, full, pol_keep);
+  if (warp >= kConsumerWarps) {
+    // ------------------------------------------------------------------ producers
+    // Producer warp pw (lane 0) issues every stage s with s % kProducerWarps == pw.
+    const int pw = warp - kConsumerWarps;
+    if (lane == 0) {
+      const uint64_t pol_stream = policy_evict_first();
+      const uint64_t pol_keep = policy_evict_last();
+      const uint32_t tx = GROUPED ? Cfg::STAGE_TX_SCALE : Cfg::STAGE_TX_NOSCALE;
+      uint32_t stage = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok;) {
+        const int ui = static_cast<int>(u);
+        const int tile = ui / units_per_tile;
+        const int ub = ui - tile * units_per_tile;
+        const long long ue_ll = ub + (u_end - u);
+        const int ue = ue_ll < units_per_tile ? static_cast<int>(ue_ll) : units_per_tile;
+        u += ue - ub;
+        const int kb = ub * ukk, ke = ue * ukk;
+        for (int kk0 = kb; kk0 < ke; kk0 += SK, ++stage) {
+          if (static_cast<int>(stage % kProducerWarps) != pw) continue;
+          const int slot = stage % D;
+          const uint32_t parity = ((stage / D) & 1u) ^ 1u;
+          if (!mbar_wait_bounded(smem_addr(&empty_bar[slot]), parity, abort_flag)) {
+            atomicOr(p.status, kStatusEmptyWaitTimeout);
+            ok = false;
+            break;
+          }
+          if (trace && stage == 0) trace[1] = global_timer_ns();
+          if (trace && blockIdx.x == 0 && stage < kTraceStages)
+            p.trace[gridDim.x * kTraceWords + stage * kTraceStageWords] = global_timer_ns();
+          const uint32_t full = smem_addr(&full_bar[slot]);
+          const uint32_t st = ring_base + slot * Cfg::STAGE;
+          mbar_arrive_expect_tx(full, tx);
+          tma_load_2d(st + Cfg::OFF_B, &p.tm_b, tile * 64 * NC, kk0, full, pol_stream);
+          tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, tile * (Cfg::M_BLK / 8) * NC, kk0, full,
+                      pol_stream);
+          if (GROUPED)
+            tma_load_2d(st + Cfg::OFF_S, &p.tm_s, tile * 16 * NC, kk0 >> 2, full, pol_keep);
+          tma_load_3d(st + Cfg::OFF_A, &p.tm_a, 0, 0, kk0 >> 1, full, pol_keep);
         }
       }
     }
@@ -184,8 +249,8 @@ __global__ void __maxnreg__(224)
   }
 
   // -------------------------------------------------------------------- consumers
-  const int cc = warp % NC;  // 64-column chunk inside the tile
-  const int kl = warp / NC;  // kk row inside a stage
+  const int cc = warp % NC;                // 64-column chunk inside the tile
+  const int kl = (warp / NC) * Cfg::RPW;  // first of this warp's 32-K rows in a stage
   const int g = lane >> 2;
   const int t = lane & 3;
   float acc[MB][4][2][4];
@@ -193,14 +258,14 @@ __global__ void __maxnreg__(224)
   bool aborted = false;
 
   for (long long u = u_begin; u < u_end;) {
-    const int tile = static_cast<int>(u / units_per_tile);
-    const int ub = static_cast<int>(u % units_per_tile);
+    const int ui = static_cast<int>(u);
+    const int tile = ui / units_per_tile;
+    const int ub = ui - tile * units_per_tile;
     const long long ue_ll = ub + (u_end - u);
-      const int ue = ue_ll < units_per_tile ? static_cast<int>(ue_ll) : units_per_tile;
+    const int ue = ue_ll < units_per_tile ? static_cast<int>(ue_ll) : units_per_tile;
     const bool first_seg = (u == u_begin);
     u += ue - ub;
-    const bool last_seg = (u == u_end);
-    const int kb = 2 * ub, ke = 2 * ue;
+    const int kb = ub * ukk, ke = ue * ukk;
 
 #pragma unroll
     for (int mb = 0; mb < MB; ++mb)
@@ -215,73 +280,100 @@ __global__ void __maxnreg__(224)
       const int rows = min(SK, ke - kk0);
       const int slot = stage % D;
       const uint32_t parity = (stage / D) & 1u;
+      unsigned long long* st_trace =
+          (trace && blockIdx.x == 0 && stage < kTraceStages && lane == 0 &&
+           (warp == 0 || warp == kConsumerWarps - 1))
+              ? p.trace + gridDim.x * kTraceWords + stage * kTraceStageWords + (warp == 0 ? 1 : 4)
+              : nullptr;
+      if (st_trace) st_trace[0] = global_timer_ns();
       if (!aborted && !mbar_wait_bounded(smem_addr(&full_bar[slot]), parity, abort_flag)) {
         aborted = true;
         if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
       }
+      if (st_trace) st_trace[1] = global_timer_ns();
       if (!aborted && kl < rows) {
         const uint32_t st = ring_base + slot * Cfg::STAGE;
-        const uint4 q = lds128(st + Cfg::OFF_B + kl * Cfg::B_ROW + cc * 512 + lane * 16);
-        uint32_t mw[2];
-        if constexpr (META3) {
-          const uint32_t mbase = st + Cfg::OFF_M + kl * Cfg::M_ROW + cc * Cfg::M_BLK;
-          const uint32_t a = lds32(mbase + lane * 4);
-          const uint32_t b = lds32(mbase + (16 + lane) * 4);
-          meta3_pair_decode(a, b, (lane & 16) != 0, mw[0], mw[1]);
-        } else {
-          ldmatrix_x2(mw, st + Cfg::OFF_M + kl * Cfg::M_ROW + cc * Cfg::M_BLK + (lane & 15) * 16);
-        }
+        // one scale row serves the warp's rows (kl is a multiple of RPW <= 2,
+        // groups are 4 rows)
         uint4 sv = make_uint4(0, 0, 0, 0);
-        if (p.grouped) {
+        if (GROUPED) {
           const int srow = ((kk0 + kl) >> 2) - (kk0 >> 2);
           sv = lds128(st + Cfg::OFF_S + srow * Cfg::S_ROW + cc * 128 + g * 16);
         }
-        uint32_t bf[MB][2][4];
-#pragma unroll
-        for (int mb = 0; mb < MB; ++mb) {
-          uint32_t r0[4], r1[4];
-          const uint32_t aaddr =
-              st + Cfg::OFF_A + (16 * mb + (lane & 15)) * Cfg::A_STRIDE + kl * 64 + (lane >> 4) * 16;
-          ldmatrix_x4(r0, aaddr);
-          ldmatrix_x4(r1, aaddr + 32);
-          bf[mb][0][0] = r0[0]; bf[mb][0][1] = r0[2]; bf[mb][0][2] = r1[0]; bf[mb][0][3] = r1[2];
-          bf[mb][1][0] = r0[1]; bf[mb][1][1] = r0[3]; bf[mb][1][2] = r1[1]; bf[mb][1][3] = r1[3];
-        }
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
         const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          half2 lo0, hi0, lo1, hi1;
-          dequant_pair(qw[j], lo0, hi0);
-          dequant_pair(qw[j] >> 8, lo1, hi1);
-          if (p.grouped) {
-            const half2 s2 = *reinterpret_cast<const half2*>(&sw[j]);
-            const half2 sx = __low2half2(s2), sy = __high2half2(s2);
-            lo0 = __hmul2(lo0, sx);
-            hi0 = __hmul2(hi0, sx);
-            lo1 = __hmul2(lo1, sy);
-            hi1 = __hmul2(hi1, sy);
+        for (int r = 0; r < Cfg::RPW; ++r) {
+          const int row = kl + r;
+          if (r > 0 && row >= rows) break;
+          const uint4 q = lds128(st + Cfg::OFF_B + row * Cfg::B_ROW + cc * 512 + lane * 16);
+          uint32_t mw[2];
+          if constexpr (META3) {
+            const uint32_t mbase = st + Cfg::OFF_M + row * Cfg::M_ROW + cc * Cfg::M_BLK;
+            const uint32_t a = lds32(mbase + lane * 4);
+            const uint32_t b = lds32(mbase + (16 + lane) * 4);
+            meta3_pair_decode(a, b, (lane & 16) != 0, mw[0], mw[1]);
+          } else {
+            ldmatrix_x2(mw, st + Cfg::OFF_M + row * Cfg::M_ROW + cc * Cfg::M_BLK + (lane & 15) * 16);
           }
-          const uint32_t af[4] = {*reinterpret_cast<uint32_t*>(&lo0), *reinterpret_cast<uint32_t*>(&lo1),
-                                  *reinterpret_cast<uint32_t*>(&hi0), *reinterpret_cast<uint32_t*>(&hi1)};
-          const uint32_t e = mw[j >> 1];
+          // activation fragments from the 128B-swizzled box: row ar, 16-byte
+          // chunk c is stored at chunk c ^ (ar & 7)
+          uint32_t bf[MB][2][4];
+          const uint32_t abox = st + Cfg::OFF_A + (row >> 1) * Cfg::A_BOX;
+          const int c0 = (row & 1) * 4 + (lane >> 4);
 #pragma unroll
           for (int mb = 0; mb < MB; ++mb) {
+            const int ar = 16 * mb + (lane & 15);
+            uint32_t r0[4], r1[4];
+            ldmatrix_x4(r0, abox + ar * 128 + ((c0 ^ (ar & 7)) << 4));
+            if (NH_LAST == 2 || mb < MB - 1) {
+              ldmatrix_x4(r1, abox + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4));
+            } else {
+              ldmatrix_x4(r1, abox + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4));
+            }
+            bf[mb][0][0] = r0[0]; bf[mb][0][1] = r0[2]; bf[mb][0][2] = r1[0]; bf[mb][0][3] = r1[2];
+            bf[mb][1][0] = r0[1]; bf[mb][1][1] = r0[3]; bf[mb][1][2] = r1[1]; bf[mb][1][3] = r1[3];
+          }
+          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (h == 1 && mb == MB - 1 && NH_LAST == 1) continue;
-              if (j & 1)
-                mma_sp_16832<1>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
-                                bf[mb][h][3], e);
-              else
-                mma_sp_16832<0>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
-                                bf[mb][h][3], e);
+          for (int j = 0; j < 4; ++j) {
+            half2 lo0, hi0, lo1, hi1;
+            dequant_pair(qw[j], lo0, hi0);
+            dequant_pair(qw[j] >> 8, lo1, hi1);
+            if (GROUPED) {
+              const half2 s2 = *reinterpret_cast<const half2*>(&sw[j]);
+              const half2 sx = __low2half2(s2), sy = __high2half2(s2);
+              lo0 = __hmul2(lo0, sx);
+              hi0 = __hmul2(hi0, sx);
+              lo1 = __hmul2(lo1, sy);
+              hi1 = __hmul2(hi1, sy);
+            }
+            const uint32_t af[4] = {*reinterpret_cast<uint32_t*>(&lo0), *reinterpret_cast<uint32_t*>(&lo1),
+                                    *reinterpret_cast<uint32_t*>(&hi0), *reinterpret_cast<uint32_t*>(&hi1)};
+            const uint32_t e = mw[j >> 1];
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (h == 1 && mb == MB - 1 && NH_LAST == 1) continue;
+                if (j & 1)
+                  mma_sp_16832<1>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
+                                  bf[mb][h][3], e);
+                else
+                  mma_sp_16832<0>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
+                                  bf[mb][h][3], e);
+              }
             }
           }
         }
       }
       __syncwarp();
+      if (st_trace) st_trace[2] = global_timer_ns();
       if (lane == 0) mbar_arrive(smem_addr(&empty_bar[slot]));
+      if (trace && threadIdx.x == 0) {
+        if (stage == 0) trace[2] = global_timer_ns();
+        trace[3] = global_timer_ns();
+        trace[5] = stage + 1;
+      }
     }
 
     // ---------------------------------------------------------------- epilogue
@@ -289,13 +381,14 @@ __global__ void __maxnreg__(224)
     //    time in increasing order (deterministic summation order).
     float4* acc4 = reinterpret_cast<float4*>(&acc[0][0][0][0]);
     float4* red4 = reinterpret_cast<float4*>(red) + cc * Cfg::ACC_F4 * 32;
-    for (int k2 = 1; k2 < SK; ++k2) {
-      if (kl == k2) {
+    const int wk = warp / NC;  // warp index among the warps sharing this chunk
+    for (int k2 = 1; k2 < kConsumerWarps / NC; ++k2) {
+      if (wk == k2) {
 #pragma unroll
         for (int v = 0; v < Cfg::ACC_F4; ++v) red4[v * 32 + lane] = acc4[v];
       }
       named_bar_sync(1, kConsumerWarps * 32);
-      if (kl == 0) {
+      if (wk == 0) {
 #pragma unroll
         for (int v = 0; v < Cfg::ACC_F4; ++v) {
           const float4 x = red4[v * 32 + lane];
@@ -304,57 +397,15 @@ __global__ void __maxnreg__(224)
       }
       named_bar_sync(1, kConsumerWarps * 32);
     }
-    if (kl != 0) continue;
 
-    // 2) leaders (one warp per chunk) finish the tile.
     const bool complete = (kb == 0 && ke == p.kk_total);
-    bool write = complete;
-    if (!complete) {
-      const long long my_slot = 2 * cta + ((first_seg) ? 0 : 1);
-      (void)last_seg;
-      float4* part = p.partials + ((my_slot * NC + cc) * Cfg::ACC_F4) * 32;
-#pragma unroll
-      for (int v = 0; v < Cfg::ACC_F4; ++v) part[v * 32 + lane] = acc4[v];
-      __threadfence();
-      named_bar_sync(2, NC * 32);
-      if (warp == 0 && lane == 0) {
-        const long long t0 = static_cast<long long>(tile) * units_per_tile;
-        const long long c_lo = unit_owner(t0, p.units, grid);
-        const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
-        const int n_part = static_cast<int>(c_hi - c_lo + 1);
-        const int prev = atomicAdd(&p.counters[tile], 1);
-        *ticket_sh = (prev == n_part - 1) ? 1 : 0;
-      }
-      named_bar_sync(2, NC * 32);
-      write = (*ticket_sh != 0);
-      if (write) {
-        __threadfence();
-        const long long t0 = static_cast<long long>(tile) * units_per_tile;
-        const long long c_lo = unit_owner(t0, p.units, grid);
-        const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
-        float4 sum[Cfg::ACC_F4];
-#pragma unroll
-        for (int v = 0; v < Cfg::ACC_F4; ++v) sum[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (long long c = c_lo; c <= c_hi; ++c) {
-          const bool started_here = unit_begin(c, p.units, grid) >= t0;
-          const long long slot = 2 * c + (started_here ? 0 : 1);
-          const float4* src = p.partials + ((slot * NC + cc) * Cfg::ACC_F4) * 32;
-#pragma unroll
-          for (int v = 0; v < Cfg::ACC_F4; ++v) {
-            const float4 x = (c == cta) ? acc4[v] : __ldcg(&src[v * 32 + lane]);
-            sum[v].x += x.x; sum[v].y += x.y; sum[v].z += x.z; sum[v].w += x.w;
-          }
-        }
-#pragma unroll
-        for (int v = 0; v < Cfg::ACC_F4; ++v) acc4[v] = sum[v];
-        if (warp == 0 && lane == 0) p.counters[tile] = 0;
-      }
-    }
-    if (write) {
-      // 3) fp32 -> fp16, per-column scale when not grouped, 16-byte stores.
+    if (complete) {
+      if (wk != 0) continue;
+      // 2a) the whole K range of the tile was reduced here: the leader warp of
+      //     each chunk converts and stores 16-byte rows of C.
       const int n0 = (tile * NC + cc) * 64 + 8 * g;
       float colscale[8];
-      if (!p.grouped) {
+      if (!GROUPED) {
         const uint4 sv = *reinterpret_cast<const uint4*>(p.s + 2ll * n0);
         const half2* sh = reinterpret_cast<const half2*>(&sv);
 #pragma unroll
@@ -377,7 +428,7 @@ __global__ void __maxnreg__(224)
               v[j] = acc[mb][j][h][e];
               v[4 + j] = acc[mb][j][h][2 + e];
             }
-            if (!p.grouped) {
+            if (!GROUPED) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[i] *= colscale[i];
             }
@@ -387,8 +438,82 @@ __global__ void __maxnreg__(224)
             for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
             *reinterpret_cast<uint4*>(p.C + static_cast<long long>(r) * p.N + n0) = o;
           }
+      continue;
+    }
+
+    // 2b) partial K range: publish this CTA's partial, take a ticket; the last
+    //     CTA of the tile sums every partial in CTA order.
+    const long long my_slot = 2 * cta + (first_seg ? 0 : 1);
+    if (wk == 0) {
+      float4* part = p.partials + ((my_slot * NC + cc) * Cfg::ACC_F4) * 32;
+#pragma unroll
+      for (int v = 0; v < Cfg::ACC_F4; ++v) part[v * 32 + lane] = acc4[v];
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    const long long t0 = static_cast<long long>(tile) * units_per_tile;
+    const long long c_lo = unit_owner(t0, p.units, grid);
+    const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
+    if (threadIdx.x == 0) {
+      fence_acq_rel_gpu();
+      const int prev = atomic_add_acq_rel(&p.counters[tile], 1);
+      *ticket_sh = (prev == static_cast<int>(c_hi - c_lo)) ? 1 : 0;
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (*ticket_sh == 0) continue;
+    if (trace && threadIdx.x == 0) trace[6] += 1;
+    fence_acq_rel_gpu();
+    // thread i handles float4 positions i, i + 256, ... of the tile's NC slots
+    constexpr int PER = (Cfg::FIX_F4 * 32 + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
+    float4 sum[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) sum[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // two participants' loads in flight at a time; summed in CTA order
+    for (long long c = c_lo; c <= c_hi; c += 2) {
+      const bool two = c + 1 <= c_hi;
+      const float4* src0 =
+          p.partials + ((2 * c + (unit_begin(c, p.units, grid) >= t0 ? 0 : 1)) * NC) * Cfg::ACC_F4 * 32;
+      const float4* src1 =
+          two ? p.partials + ((2 * (c + 1) + (unit_begin(c + 1, p.units, grid) >= t0 ? 0 : 1)) * NC) *
+                                 Cfg::ACC_F4 * 32
+              : src0;
+      float4 x0[PER], x1[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int pos = threadIdx.x + i * kConsumerWarps * 32;
+        const bool in = pos < Cfg::FIX_F4 * 32;
+        x0[i] = in ? __ldcg(src0 + pos) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x1[i] = (in && two) ? __ldcg(src1 + pos) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        sum[i].x += x0[i].x; sum[i].y += x0[i].y; sum[i].z += x0[i].z; sum[i].w += x0[i].w;
+        if (two) {
+          sum[i].x += x1[i].x; sum[i].y += x1[i].y; sum[i].z += x1[i].z; sum[i].w += x1[i].w;
+        }
+      }
+    }
+    if (threadIdx.x == 0) p.counters[tile] = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int pos = threadIdx.x + i * kConsumerWarps * 32;
+      if (pos >= Cfg::FIX_F4 * 32) continue;
+      const int ch = pos / (Cfg::ACC_F4 * 32);
+      const int v = (pos / 32) % Cfg::ACC_F4;
+      const int ln = pos % 32;
+      const float vals[4] = {sum[i].x, sum[i].y, sum[i].z, sum[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int nc, row;
+        acc_coords(v, ln, e, nc, row);
+        if (row >= p.M) continue;
+        const int n = (tile * NC + ch) * 64 + nc;
+        float val = vals[e];
+        if (!GROUPED) val *= __half2float(reinterpret_cast<const half*>(p.s)[n]);
+        p.C[static_cast<long long>(row) * p.N + n] = __float2half_rn(val);
+      }
     }
   }
+  if (trace && threadIdx.x == 0) trace[4] = global_timer_ns();
 }
 
 }  // namespace sm100

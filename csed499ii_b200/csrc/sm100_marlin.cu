@@ -5,9 +5,12 @@
 // (kernel_experiments/sparse_marlin/src/marlin/marlin_cuda_kernel_nm.cu:751-830)
 // so that shapes it rejects are rejected with the same status; the kernel
 // tiling behind it is this library's own.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -26,6 +29,9 @@ __device__ int g_device_status = 0;
 namespace {
 
 thread_local std::string t_last_cuda_error;
+
+// Device buffer for per-CTA timelines (only written by SM100_MARLIN_TRACE builds).
+unsigned long long* g_trace_buffer = nullptr;
 
 int cuda_fail(cudaError_t e) {
   t_last_cuda_error = cudaGetErrorString(e);
@@ -96,31 +102,147 @@ int device_sms(int dev, int* sms) {
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
-int choose_nc(int n_out) { return (n_out % 256 == 0) ? 4 : ((n_out % 128 == 0) ? 2 : 1); }
+// Column-tile width (in 64-column chunks).  Wider tiles re-read the
+// activations less often; narrower tiles leave fewer CTAs sharing one tile,
+// which bounds the split-K fixup (its cost grows with the CTAs per tile).
+// Picks the widest tile with at most four CTAs per tile.
+// SM100_MARLIN_NC=1|2|4 overrides (tuning knob).
+int choose_nc(int n_out, int sms) {
+  static const int forced = [] {
+    const char* e = std::getenv("SM100_MARLIN_NC");
+    return e ? std::atoi(e) : 0;
+  }();
+  const int chunks = n_out / 64;
+  if ((forced == 1 || forced == 2 || forced == 4) && chunks % forced == 0) return forced;
+  for (int nc : {4, 2}) {
+    if (chunks % nc) continue;
+    const int tiles = chunks / nc;
+    const int per_tile = (sms + tiles - 1) / tiles;
+    if (per_tile <= 4) return nc;
+  }
+  return 1;
+}
 
 struct Plan {
-  int nc, mb, nh_last, grid;
+  int nc, mb, nh_last, grid, unit_kk, sk;
   long long units;
   size_t scratch;
 };
 
 Plan make_plan(int n_out, int m_rows, int k_in, int sms) {
   Plan pl;
-  pl.nc = choose_nc(n_out);
+  pl.nc = choose_nc(n_out, sms);
   pl.mb = (m_rows + 15) / 16;
-  pl.nh_last = (m_rows - 16 * (pl.mb - 1)) > 8 ? 2 : 1;
+  if (pl.mb == 3) pl.mb = 4;
+  pl.nh_last = (pl.mb == 1 && m_rows <= 8) ? 1 : 2;
+  pl.sk = kConsumerWarps * rows_per_warp(pl.nc, pl.mb) / pl.nc;
+  const int kk = k_in / 32;
+  // A unit is one full stage (8 blocks of 32 K x 64 columns) when K allows
+  // it; scale groups (4 rows) stay aligned to stage starts.
+  pl.unit_kk = 2;
+  for (int u = pl.sk; u >= 4; u /= 2)
+    if (kk % u == 0) {
+      pl.unit_kk = u;
+      break;
+    }
   const long long n_tiles = n_out / (64 * pl.nc);
-  pl.units = n_tiles * (k_in / 64);
+  pl.units = n_tiles * (kk / pl.unit_kk);
   pl.grid = static_cast<int>(pl.units < sms ? pl.units : sms);
   pl.scratch = static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 8192;
   return pl;
 }
 
-template <int NC, int MB, int NH, bool META3>
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int encode_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+              const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+              CUtensorMapSwizzle swizzle) {
+  auto enc = tensor_map_encoder();
+  if (!enc) {
+    t_last_cuda_error = "cuTensorMapEncodeTiled unavailable";
+    return SM100_MARLIN_ERR_CUDA;
+  }
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t b[3], es[3];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = enc(map, dtype, rank, const_cast<void*>(base), d, st, b, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")";
+    return SM100_MARLIN_ERR_CUDA;
+  }
+  return SM100_MARLIN_OK;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle) {
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return encode_nd(map, dtype, base, 2, dims, strides, box, swizzle);
+}
+
+// Fills the four tensor maps of `p` for this launch's plan.
+int encode_maps(GemmParams& p, const Plan& pl, const void* A, const void* B, const void* meta,
+                const void* s, int meta_bits) {
+  const int nc = pl.nc, sk = pl.sk;
+  const uint64_t N = p.N, K = p.K, KK = K / 32;
+  // activations as (64 halves, M rows, K/64 slices): one box per stage holds
+  // the SK/2 64-wide K slices of all (padded) rows, 128B-swizzled
+  const uint64_t a_dims[3] = {64, static_cast<uint64_t>(p.M), K / 64};
+  const uint64_t a_strides[2] = {2 * K, 128};
+  const uint32_t a_box[3] = {64, static_cast<uint32_t>(16 * pl.mb), static_cast<uint32_t>(sk / 2)};
+  int rc = encode_nd(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, 3, a_dims, a_strides, a_box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, KK, 8 * N, 64 * nc, sk,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (meta_bits == 3)
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, 3 * N / 8, KK, 3 * N,
+                   24 * nc, sk, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, KK, 4 * N, 32 * nc,
+                   sk, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (p.grouped) {
+    const uint32_t s_rows = sk / 4;
+    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 16 * nc,
+                   s_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    std::memset(&p.tm_s, 0, sizeof(p.tm_s));
+  }
+  return SM100_MARLIN_OK;
+}
+
+template <int NC, int MB, int NH, bool META3, bool GROUPED>
 int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
   using Cfg = DecodeCfg<NC, MB, META3>;
   static bool attr_set[64] = {};
-  auto kern = marlin24_decode_kernel<NC, MB, NH, META3>;
+  auto kern = marlin24_decode_kernel<NC, MB, NH, META3, GROUPED>;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -131,19 +253,15 @@ int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
-template <bool META3>
-int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
-#define SM100_CASE(NC_, MB_, NH_)                                   \
-  if (pl.nc == NC_ && pl.mb == MB_ && pl.nh_last == NH_)            \
-    return launch_one<NC_, MB_, NH_, META3>(p, pl.grid, dev, stream);
+template <bool META3, bool GROUPED>
+int dispatch_g(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
+#define SM100_CASE(NC_, MB_, NH_)                                            \
+  if (pl.nc == NC_ && pl.mb == MB_ && pl.nh_last == NH_)                     \
+    return launch_one<NC_, MB_, NH_, META3, GROUPED>(p, pl.grid, dev, stream);
 #define SM100_CASES_NC(NC_) \
   SM100_CASE(NC_, 1, 1)     \
   SM100_CASE(NC_, 1, 2)     \
-  SM100_CASE(NC_, 2, 1)     \
   SM100_CASE(NC_, 2, 2)     \
-  SM100_CASE(NC_, 3, 1)     \
-  SM100_CASE(NC_, 3, 2)     \
-  SM100_CASE(NC_, 4, 1)     \
   SM100_CASE(NC_, 4, 2)
   SM100_CASES_NC(4)
   SM100_CASES_NC(2)
@@ -151,6 +269,12 @@ int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) 
 #undef SM100_CASES_NC
 #undef SM100_CASE
   return SM100_MARLIN_ERR_KERN_SHAPE;
+}
+
+template <bool META3>
+int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
+  return p.grouped ? dispatch_g<META3, true>(p, pl, dev, stream)
+                   : dispatch_g<META3, false>(p, pl, dev, stream);
 }
 
 // Reference shape rules (marlin_cuda_kernel_nm.cu:763-783,811-823).
@@ -218,9 +342,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     const int rows = (prob_n - r0) < 64 ? (prob_n - r0) : 64;
     Plan pl = make_plan(prob_m, rows, prob_k, sms);
     GemmParams p;
-    p.A = static_cast<const uint8_t*>(A) + static_cast<size_t>(r0) * prob_k * 2;
-    p.B = static_cast<const uint8_t*>(B);
-    p.meta = static_cast<const uint8_t*>(meta);
+    const uint8_t* a_rows = static_cast<const uint8_t*>(A) + static_cast<size_t>(r0) * prob_k * 2;
     p.s = static_cast<const uint8_t*>(s);
     p.C = reinterpret_cast<half*>(static_cast<uint8_t*>(C) + static_cast<size_t>(r0) * prob_m * 2);
     p.partials = static_cast<float4*>(scratch);
@@ -230,9 +352,12 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.N = prob_m;
     p.K = prob_k;
     p.grouped = groupsize != -1 ? 1 : 0;
-    p.n_tiles = prob_m / (64 * pl.nc);
     p.kk_total = prob_k / 32;
+    p.unit_kk = pl.unit_kk;
     p.units = pl.units;
+    p.trace = g_trace_buffer;
+    rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
+    if (rc != SM100_MARLIN_OK) return rc;
     rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream) : dispatch<false>(p, pl, dev, stream);
     if (rc != SM100_MARLIN_OK) return rc;
   }
@@ -359,5 +484,10 @@ const char* sm100_marlin_error_string(int code) {
 }
 
 const char* sm100_marlin_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
+
+int sm100_marlin_set_trace_buffer(void* buf) {
+  g_trace_buffer = static_cast<unsigned long long*>(buf);
+  return SM100_MARLIN_TRACE ? SM100_MARLIN_OK : SM100_MARLIN_ERR_ARGUMENT;
+}
 
 }  // extern "C"

@@ -117,6 +117,14 @@ const char* sm100_marlin_error_string(int code);
 /* Message of the last CUDA error seen by this library on this thread. */
 const char* sm100_marlin_last_cuda_error(void);
 
+/* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 every GEMM
+ * launch writes 8 uint64 words per CTA into `buf` (device memory, >= grid*64
+ * bytes, zeroed by the caller): %globaltimer at kernel entry, first TMA issue,
+ * first and last stage consumed, end of the CTA, stage count, fixup count.
+ * Returns SM100_MARLIN_ERR_ARGUMENT in normal builds (nothing is recorded).
+ * No counterpart in the reference (its profiling is external, via ncu). */
+int sm100_marlin_set_trace_buffer(void* buf);
+
 #ifdef __cplusplus
 }
 #endif
