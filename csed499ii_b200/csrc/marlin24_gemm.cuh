@@ -37,6 +37,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "device_primitives.cuh"
 
 namespace sm100 {
@@ -66,30 +68,43 @@ struct GemmParams {
 // TMA issue, first stage consumed, last stage consumed, end of epilogue, and
 // the number of stages and fixups of the CTA.
 constexpr int kTraceWords = 8;
-// CTA 0 additionally records per-stage times after the per-CTA words:
-// [stage][0] producer issue, [1..3] consumer warp 0 wait start / data ready /
-// done, [4..6] the same for the last consumer warp.
+// CTA 0 additionally records per-stage SM clock cycles (clock64, cheap to
+// read) after the per-CTA words: [stage][0] producer issue, [1..3] consumer
+// warp 0 wait start / data ready / done, [4..6] the same for the last
+// consumer warp, [7] the CTA's clock at entry (for the offsets).
 constexpr int kTraceStages = 64;
 constexpr int kTraceStageWords = 8;
 #ifndef SM100_MARLIN_TRACE
 #define SM100_MARLIN_TRACE 0
 #endif
 
-constexpr int kConsumerWarps = 8;
-constexpr int kProducerWarps = 4;
+// Warp roles per configuration: 8 consumer warps; 2 producer warps for batch
+// rows <= 16 (24 KB weight stages) and 4 for larger batches (smaller stages).
+constexpr int consumer_warps(int mb) { return 8; }
+constexpr int producer_warps(int nc, int mb) { return (mb == 1 || (nc == 1 && mb == 4)) ? 2 : 4; }
 // Consecutive 32-K rows of one chunk per consumer warp per stage: 2, except
 // for narrow tiles with many batch rows (64 columns above 16 rows, 128 columns
 // at 64 rows), whose activation slices would not fit a useful ring.
 constexpr int rows_per_warp(int nc, int mb) {
-  return ((nc == 1 && mb > 1) || (nc == 2 && mb == 4)) ? 1 : 2;
+  return mb == 1 ? 4 : (((nc == 1 && mb > 1) || (nc == 2 && mb == 4)) ? 1 : 2);
 }
-constexpr int kThreads = (kConsumerWarps + kProducerWarps) * 32;
-constexpr int kSmemBudget = 200 * 1024;
+// With one 16-row batch block a warp owns a whole 128-K scale group per
+// stage: its four row products go to a temporary fp32 accumulator that is
+// scaled once per group (instead of scaling every dequantised weight in
+// fp16).  Measured faster than per-weight scaling in the full kernel.
+constexpr bool scale_on_accumulator(int mb) { return mb == 1; }
+
+constexpr int kSmemBudget = 227 * 1024;
 
 template <int NC, int MB, bool META3>
 struct DecodeCfg {
+  static constexpr int CW = consumer_warps(MB);
+  static constexpr int PW = producer_warps(NC, MB);
+  static constexpr int THREADS = (CW + PW) * 32;
+  static constexpr int WPC = CW / NC;                            // consumer warps per chunk
   static constexpr int RPW = rows_per_warp(NC, MB);
-  static constexpr int SK = kConsumerWarps * RPW / NC;           // 32-K rows per stage
+  static constexpr bool SCALE_ACC = scale_on_accumulator(MB);
+  static constexpr int SK = CW * RPW / NC;                       // 32-K rows per stage
   static constexpr int B_ROW = 512 * NC;                         // bytes of B per row
   static constexpr int M_BLK = META3 ? 192 : 256;                // meta bytes per (row, chunk)
   static constexpr int M_ROW = M_BLK * NC;
@@ -104,19 +119,22 @@ struct DecodeCfg {
   static constexpr int STAGE_RAW = OFF_S + S_ROWS * S_ROW;
   static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int ACC_F4 = 8 * MB;                          // float4 per thread of acc
-  static constexpr int RED_BYTES = NC * ACC_F4 * 32 * 16;        // one slot per chunk
+  static constexpr int RED_SLOTS = 1;                            // reduction slots per chunk
+  static constexpr int RED_BYTES = NC * RED_SLOTS * ACC_F4 * 32 * 16;
   static constexpr int HEADER = 1024;                            // barriers + flags
   static constexpr int RING_OFF = (HEADER + RED_BYTES + 1023) / 1024 * 1024;
   static constexpr int DEPTH_FIT = (kSmemBudget - RING_OFF - 1024) / STAGE;
   static constexpr int DEPTH_RAW = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
-  static constexpr int DEPTH = DEPTH_RAW / kProducerWarps * kProducerWarps;  // slots per producer equal
+  static constexpr int DEPTH = DEPTH_RAW / PW * PW;              // slots per producer equal
   static constexpr int SMEM = RING_OFF + DEPTH * STAGE + 1024;   // +1024: base alignment slack
   static constexpr uint32_t STAGE_TX_NOSCALE = A_BOXES * A_BOX + SK * (B_ROW + M_ROW);
-  static_assert(DEPTH >= kProducerWarps, "ring too shallow for the producer warps");
+  static_assert(DEPTH >= PW, "ring too shallow for the producer warps");
   static constexpr uint32_t STAGE_TX_SCALE = STAGE_TX_NOSCALE + S_ROWS * S_ROW;
-  static constexpr int FIX_F4 = NC * ACC_F4;                     // float4 per thread in the fixup
-  static_assert(DEPTH >= 4, "ring too shallow");
+  static constexpr int FIX_F4 = NC * ACC_F4;                     // float4 of a tile per lane
+  static_assert(DEPTH >= 2, "ring too shallow");
   static_assert(SK % 4 == 0, "stage must hold whole scale groups");
+  static_assert(!SCALE_ACC || RPW == 4, "accumulator scaling needs whole groups per warp");
+  static_assert(THREADS <= 1024, "too many threads");
 };
 
 // floor(num / den) for 0 <= num < 2^53, den > 0, without the slow 64-bit
@@ -158,11 +176,13 @@ __device__ __forceinline__ void acc_coords(int v, int lane, int e, int& n_in_chu
 }
 
 template <int NC, int MB, int NH_LAST, bool META3, bool GROUPED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     marlin24_decode_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = DecodeCfg<NC, MB, META3>;
   constexpr int SK = Cfg::SK;
   constexpr int D = Cfg::DEPTH;
+  constexpr int kConsumerWarps = Cfg::CW;
+  constexpr int kProducerWarps = Cfg::PW;
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the ring (128B-swizzle atoms).
@@ -179,7 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   unsigned long long* trace =
       SM100_MARLIN_TRACE && p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceWords : nullptr;
-  if (trace && threadIdx.x == 0) trace[0] = global_timer_ns();
+  if (trace && threadIdx.x == 0) {
+    trace[0] = global_timer_ns();
+    if (blockIdx.x == 0) p.trace[gridDim.x * kTraceWords + 7] = clock64();
+  }
 
   if (threadIdx.x < D) {
     mbar_init(smem_addr(&full_bar[threadIdx.x]), 1);
@@ -205,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= kConsumerWarps) {
     // ------------------------------------------------------------------ producers
-    // Producer warp pw (lane 0) issues every stage s with s % kProducerWarps == pw.
+    // Producer warp pw (lane 0) issues every stage s with s % PW == pw.
     const int pw = warp - kConsumerWarps;
     if (lane == 0) {
       const uint64_t pol_stream = policy_evict_first();
@@ -232,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (trace && stage == 0) trace[1] = global_timer_ns();
           if (trace && blockIdx.x == 0 && stage < kTraceStages)
-            p.trace[gridDim.x * kTraceWords + stage * kTraceStageWords] = global_timer_ns();
+            p.trace[gridDim.x * kTraceWords + stage * kTraceStageWords] = clock64();
           const uint32_t full = smem_addr(&full_bar[slot]);
           const uint32_t st = ring_base + slot * Cfg::STAGE;
           mbar_arrive_expect_tx(full, tx);
@@ -256,6 +279,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   float acc[MB][4][2][4];
   uint32_t stage = 0;
   bool aborted = false;
+
+  // Per-warp shared-memory offsets inside a stage, computed once: every
+  // per-stage load is then (stage base + constant) with an immediate row
+  // offset.  Activations: row ar of the 128B-swizzled box keeps 16-byte chunk
+  // c at chunk c ^ (ar & 7); a_off[p][mb][i] is the chunk holding K 16i..16i+7
+  // (lanes 0-15) / 16i+8..16i+15 (lanes 16-31) of a row with parity p.
+  const uint32_t b_off = Cfg::OFF_B + kl * Cfg::B_ROW + cc * 512 + lane * 16;
+  const uint32_t m_off = Cfg::OFF_M + kl * Cfg::M_ROW + cc * Cfg::M_BLK +
+                         (META3 ? lane * 4 : (lane & 15) * 16);
+  const uint32_t s_off = Cfg::OFF_S + (kl >> 2) * Cfg::S_ROW + cc * 128 + g * 16;
+  uint32_t a_off[2][MB][2];
+#pragma unroll
+  for (int par = 0; par < 2; ++par)
+#pragma unroll
+    for (int mb = 0; mb < MB; ++mb) {
+      const int ar = 16 * mb + (lane & 15);
+      const int c0 = par * 4 + (lane >> 4);
+      a_off[par][mb][0] = Cfg::OFF_A + (kl >> 1) * Cfg::A_BOX + ar * 128 + ((c0 ^ (ar & 7)) << 4);
+      a_off[par][mb][1] =
+          Cfg::OFF_A + (kl >> 1) * Cfg::A_BOX + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4);
+    }
 
   for (long long u = u_begin; u < u_end;) {
     const int ui = static_cast<int>(u);
@@ -285,89 +329,114 @@ __global__ void __launch_bounds__(kThreads, 1)
            (warp == 0 || warp == kConsumerWarps - 1))
               ? p.trace + gridDim.x * kTraceWords + stage * kTraceStageWords + (warp == 0 ? 1 : 4)
               : nullptr;
-      if (st_trace) st_trace[0] = global_timer_ns();
+      if (st_trace) st_trace[0] = clock64();
       if (!aborted && !mbar_wait_bounded(smem_addr(&full_bar[slot]), parity, abort_flag)) {
         aborted = true;
         if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
       }
-      if (st_trace) st_trace[1] = global_timer_ns();
+      if (st_trace) st_trace[1] = clock64();
       if (!aborted && kl < rows) {
         const uint32_t st = ring_base + slot * Cfg::STAGE;
-        // one scale row serves the warp's rows (kl is a multiple of RPW <= 2,
-        // groups are 4 rows)
+        const int nr = min(Cfg::RPW, rows - kl);  // rows of this warp in this stage
+        // one scale row serves the warp's rows (kl is a multiple of RPW, stage
+        // starts are multiples of 4 when grouped, groups are 4 rows)
         uint4 sv = make_uint4(0, 0, 0, 0);
-        if (GROUPED) {
-          const int srow = ((kk0 + kl) >> 2) - (kk0 >> 2);
-          sv = lds128(st + Cfg::OFF_S + srow * Cfg::S_ROW + cc * 128 + g * 16);
-        }
+        if (GROUPED) sv = lds128(st + s_off);
         const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+        constexpr bool kTmp = GROUPED && Cfg::SCALE_ACC;
+        float tmp[kTmp ? MB : 1][4][2][4];
+        auto rows_body = [&](auto full) {
+          constexpr bool kFull = decltype(full)::value;
 #pragma unroll
-        for (int r = 0; r < Cfg::RPW; ++r) {
-          const int row = kl + r;
-          if (r > 0 && row >= rows) break;
-          const uint4 q = lds128(st + Cfg::OFF_B + row * Cfg::B_ROW + cc * 512 + lane * 16);
-          uint32_t mw[2];
-          if constexpr (META3) {
-            const uint32_t mbase = st + Cfg::OFF_M + row * Cfg::M_ROW + cc * Cfg::M_BLK;
-            const uint32_t a = lds32(mbase + lane * 4);
-            const uint32_t b = lds32(mbase + (16 + lane) * 4);
-            meta3_pair_decode(a, b, (lane & 16) != 0, mw[0], mw[1]);
-          } else {
-            ldmatrix_x2(mw, st + Cfg::OFF_M + row * Cfg::M_ROW + cc * Cfg::M_BLK + (lane & 15) * 16);
-          }
-          // activation fragments from the 128B-swizzled box: row ar, 16-byte
-          // chunk c is stored at chunk c ^ (ar & 7)
-          uint32_t bf[MB][2][4];
-          const uint32_t abox = st + Cfg::OFF_A + (row >> 1) * Cfg::A_BOX;
-          const int c0 = (row & 1) * 4 + (lane >> 4);
-#pragma unroll
-          for (int mb = 0; mb < MB; ++mb) {
-            const int ar = 16 * mb + (lane & 15);
-            uint32_t r0[4], r1[4];
-            ldmatrix_x4(r0, abox + ar * 128 + ((c0 ^ (ar & 7)) << 4));
-            if (NH_LAST == 2 || mb < MB - 1) {
-              ldmatrix_x4(r1, abox + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4));
+          for (int r = 0; r < Cfg::RPW; ++r) {
+            if (!kFull && r >= nr) break;
+            const uint4 q = lds128(st + b_off + r * Cfg::B_ROW);
+            uint32_t mw[2];
+            if constexpr (META3) {
+              const uint32_t a = lds32(st + m_off + r * Cfg::M_ROW);
+              const uint32_t b = lds32(st + m_off + r * Cfg::M_ROW + 64);
+              meta3_pair_decode(a, b, (lane & 16) != 0, mw[0], mw[1]);
             } else {
-              ldmatrix_x4(r1, abox + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4));
+              ldmatrix_x2(mw, st + m_off + r * Cfg::M_ROW);
             }
-            bf[mb][0][0] = r0[0]; bf[mb][0][1] = r0[2]; bf[mb][0][2] = r1[0]; bf[mb][0][3] = r1[2];
-            bf[mb][1][0] = r0[1]; bf[mb][1][1] = r0[3]; bf[mb][1][2] = r1[1]; bf[mb][1][3] = r1[3];
-          }
-          const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            half2 lo0, hi0, lo1, hi1;
-            dequant_pair(qw[j], lo0, hi0);
-            dequant_pair(qw[j] >> 8, lo1, hi1);
-            if (GROUPED) {
-              const half2 s2 = *reinterpret_cast<const half2*>(&sw[j]);
-              const half2 sx = __low2half2(s2), sy = __high2half2(s2);
-              lo0 = __hmul2(lo0, sx);
-              hi0 = __hmul2(hi0, sx);
-              lo1 = __hmul2(lo1, sy);
-              hi1 = __hmul2(hi1, sy);
-            }
-            const uint32_t af[4] = {*reinterpret_cast<uint32_t*>(&lo0), *reinterpret_cast<uint32_t*>(&lo1),
-                                    *reinterpret_cast<uint32_t*>(&hi0), *reinterpret_cast<uint32_t*>(&hi1)};
-            const uint32_t e = mw[j >> 1];
+            // row parity / box index: compile-time when kl is even (RPW even)
+            const int par = (Cfg::RPW % 2 == 0) ? (r & 1) : ((kl + r) & 1);
+            const uint32_t abox = st + (((kl & 1) + r) >> 1) * Cfg::A_BOX;
+            uint32_t bf[MB][2][4];
 #pragma unroll
             for (int mb = 0; mb < MB; ++mb) {
+              uint32_t r0[4], r1[4];
+              ldmatrix_x4(r0, abox + (par ? a_off[1][mb][0] : a_off[0][mb][0]));
+              ldmatrix_x4(r1, abox + (par ? a_off[1][mb][1] : a_off[0][mb][1]));
+              bf[mb][0][0] = r0[0]; bf[mb][0][1] = r0[2]; bf[mb][0][2] = r1[0]; bf[mb][0][3] = r1[2];
+              bf[mb][1][0] = r0[1]; bf[mb][1][1] = r0[3]; bf[mb][1][2] = r1[1]; bf[mb][1][3] = r1[3];
+            }
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              half2 lo0, hi0, lo1, hi1;
+              dequant_pair(qw[j], lo0, hi0);
+              dequant_pair(qw[j] >> 8, lo1, hi1);
+              if (GROUPED && !kTmp) {
+                const half2 s2 = *reinterpret_cast<const half2*>(&sw[j]);
+                const half2 sx = __low2half2(s2), sy = __high2half2(s2);
+                lo0 = __hmul2(lo0, sx);
+                hi0 = __hmul2(hi0, sx);
+                lo1 = __hmul2(lo1, sy);
+                hi1 = __hmul2(hi1, sy);
+              }
+              const uint32_t af[4] = {*reinterpret_cast<uint32_t*>(&lo0), *reinterpret_cast<uint32_t*>(&lo1),
+                                      *reinterpret_cast<uint32_t*>(&hi0), *reinterpret_cast<uint32_t*>(&hi1)};
+              const uint32_t e = mw[j >> 1];
+#pragma unroll
+              for (int mb = 0; mb < MB; ++mb) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  if (h == 1 && mb == MB - 1 && NH_LAST == 1) continue;
+                  float(&d)[4] = kTmp ? tmp[kTmp ? mb : 0][j][h] : acc[mb][j][h];
+                  if (kTmp && r == 0) {
+                    if (j & 1)
+                      mma_sp_16832_z<1>(d, af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2], bf[mb][h][3], e);
+                    else
+                      mma_sp_16832_z<0>(d, af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2], bf[mb][h][3], e);
+                  } else {
+                    if (j & 1)
+                      mma_sp_16832<1>(d, af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2], bf[mb][h][3], e);
+                    else
+                      mma_sp_16832<0>(d, af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2], bf[mb][h][3], e);
+                  }
+                }
+              }
+            }
+          }
+        };
+        if (nr == Cfg::RPW)
+          rows_body(std::true_type{});
+        else
+          rows_body(std::false_type{});
+        if constexpr (kTmp) {
+          // acc += s (group scale of the output column) * tmp, in fp32.
+          // frag_s[j] = (scale of out-feature 8g+j, of 8g+j+4): x for the
+          // accumulator rows g (elements 0,1), y for rows g+8 (elements 2,3).
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const half2 s2 = *reinterpret_cast<const half2*>(&sw[j]);
+            const float sx = __low2float(s2), sy = __high2float(s2);
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb)
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 if (h == 1 && mb == MB - 1 && NH_LAST == 1) continue;
-                if (j & 1)
-                  mma_sp_16832<1>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
-                                  bf[mb][h][3], e);
-                else
-                  mma_sp_16832<0>(acc[mb][j][h], af, bf[mb][h][0], bf[mb][h][1], bf[mb][h][2],
-                                  bf[mb][h][3], e);
+                acc[mb][j][h][0] = fmaf(sx, tmp[mb][j][h][0], acc[mb][j][h][0]);
+                acc[mb][j][h][1] = fmaf(sx, tmp[mb][j][h][1], acc[mb][j][h][1]);
+                acc[mb][j][h][2] = fmaf(sy, tmp[mb][j][h][2], acc[mb][j][h][2]);
+                acc[mb][j][h][3] = fmaf(sy, tmp[mb][j][h][3], acc[mb][j][h][3]);
               }
-            }
           }
         }
       }
       __syncwarp();
-      if (st_trace) st_trace[2] = global_timer_ns();
+      if (st_trace) st_trace[2] = clock64();
       if (lane == 0) mbar_arrive(smem_addr(&empty_bar[slot]));
       if (trace && threadIdx.x == 0) {
         if (stage == 0) trace[2] = global_timer_ns();
@@ -377,12 +446,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---------------------------------------------------------------- epilogue
-    // 1) reduce the SK warps of each chunk through shared memory, one kl at a
-    //    time in increasing order (deterministic summation order).
+    // 1) reduce the WPC warps of each chunk through shared memory, adding
+    //    warp wk = 1, 2, ... to warp 0 in turn (fixed summation order; one
+    //    slot per chunk keeps the smem for the ring).
     float4* acc4 = reinterpret_cast<float4*>(&acc[0][0][0][0]);
-    float4* red4 = reinterpret_cast<float4*>(red) + cc * Cfg::ACC_F4 * 32;
     const int wk = warp / NC;  // warp index among the warps sharing this chunk
-    for (int k2 = 1; k2 < kConsumerWarps / NC; ++k2) {
+    float4* red4 = reinterpret_cast<float4*>(red) + (cc * Cfg::ACC_F4) * 32;
+    for (int k2 = 1; k2 < Cfg::WPC; ++k2) {
       if (wk == k2) {
 #pragma unroll
         for (int v = 0; v < Cfg::ACC_F4; ++v) red4[v * 32 + lane] = acc4[v];

@@ -135,7 +135,7 @@ Plan make_plan(int n_out, int m_rows, int k_in, int sms) {
   pl.mb = (m_rows + 15) / 16;
   if (pl.mb == 3) pl.mb = 4;
   pl.nh_last = (pl.mb == 1 && m_rows <= 8) ? 1 : 2;
-  pl.sk = kConsumerWarps * rows_per_warp(pl.nc, pl.mb) / pl.nc;
+  pl.sk = consumer_warps(pl.mb) * rows_per_warp(pl.nc, pl.mb) / pl.nc;
   const int kk = k_in / 32;
   // A unit is one full stage (8 blocks of 32 K x 64 columns) when K allows
   // it; scale groups (4 rows) stay aligned to stage starts.
@@ -248,7 +248,7 @@ int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
     if (e != cudaSuccess) return cuda_fail(e);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<grid, kThreads, Cfg::SMEM, stream>>>(p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
