@@ -37,6 +37,7 @@ SIGNATURES = {
     "sm100_marlin_error_string": (ctypes.c_char_p, [_c_int]),
     "sm100_marlin_last_cuda_error": (ctypes.c_char_p, []),
     "sm100_marlin_set_trace_buffer": (_c_int, [_vp]),
+    "sm100_marlin_set_overlap": (_c_int, [_c_int]),
 }
 
 OK = 0

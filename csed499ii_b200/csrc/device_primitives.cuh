@@ -150,6 +150,21 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  launch_dependents lets the next kernel of
+// the stream (launched with the programmatic-serialization attribute) begin
+// once every CTA of this grid has issued it; wait blocks until the previous
+// grid has completed and its memory operations are visible.  Both are no-ops
+// for kernels launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dependency_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Named barriers for subsets of warps (id 0 is __syncthreads).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {

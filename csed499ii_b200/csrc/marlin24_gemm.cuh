@@ -61,6 +61,7 @@ struct GemmParams {
   int unit_kk;          // 32-K rows per unit (2, 4 or 8); divides kk_total
   long long units;      // n_tiles * kk_total / unit_kk
   unsigned long long* trace;  // optional per-CTA timestamps (SM100_MARLIN_TRACE builds)
+  int pdl;              // launched with programmatic dependent launch
 };
 
 // Per-CTA timeline written when the library is built with
@@ -210,6 +211,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     fence_mbar_init();
   }
   if (threadIdx.x == 0) *abort_flag = 0;
+  // Let the next kernel on the stream start its prologue and weight prefetch
+  // while this one runs (it waits for this grid before touching anything
+  // this kernel reads or writes besides the weights).
+  if (p.pdl && threadIdx.x == 0) grid_dependency_launch();
   if (threadIdx.x == kConsumerWarps * 32) {
     prefetch_tmap(&p.tm_a);
     prefetch_tmap(&p.tm_b);
@@ -234,6 +239,26 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       const uint64_t pol_stream = policy_evict_first();
       const uint64_t pol_keep = policy_evict_last();
       const uint32_t tx = GROUPED ? Cfg::STAGE_TX_SCALE : Cfg::STAGE_TX_NOSCALE;
+      // With programmatic dependent launch the previous kernel on the stream
+      // may still be running: the weight parts of this warp's first stages
+      // (at most one ring's worth) are issued before griddepcontrol.wait; the
+      // activation parts, which the previous kernel may have produced, only
+      // after it.
+      constexpr int kPre = D / kProducerWarps;
+      int pre_slot[kPre], pre_kk[kPre];
+      int n_pre = 0;
+      bool waited = !p.pdl;
+      auto issue_a = [&](int slot, int kk0) {
+        const uint32_t full = smem_addr(&full_bar[slot]);
+        tma_load_3d(ring_base + slot * Cfg::STAGE + Cfg::OFF_A, &p.tm_a, 0, 0, kk0 >> 1, full,
+                    pol_keep);
+      };
+      auto release_deferred = [&]() {
+        grid_dependency_wait();
+        waited = true;
+        for (int i = 0; i < n_pre; ++i) issue_a(pre_slot[i], pre_kk[i]);
+        n_pre = 0;
+      };
       uint32_t stage = 0;
       bool ok = true;
       for (long long u = u_begin; u < u_end && ok;) {
@@ -248,6 +273,9 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
           if (static_cast<int>(stage % kProducerWarps) != pw) continue;
           const int slot = stage % D;
           const uint32_t parity = ((stage / D) & 1u) ^ 1u;
+          // a slot can only be free again after its stage was consumed, which
+          // needs the deferred activation loads: release them first
+          if (!waited && n_pre == kPre) release_deferred();
           if (!mbar_wait_bounded(smem_addr(&empty_bar[slot]), parity, abort_flag)) {
             atomicOr(p.status, kStatusEmptyWaitTimeout);
             ok = false;
@@ -264,9 +292,16 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
                       pol_stream);
           if (GROUPED)
             tma_load_2d(st + Cfg::OFF_S, &p.tm_s, tile * 16 * NC, kk0 >> 2, full, pol_keep);
-          tma_load_3d(st + Cfg::OFF_A, &p.tm_a, 0, 0, kk0 >> 1, full, pol_keep);
+          if (waited) {
+            issue_a(slot, kk0);
+          } else {
+            pre_slot[n_pre] = slot;
+            pre_kk[n_pre] = kk0;
+            ++n_pre;
+          }
         }
       }
+      if (!waited) release_deferred();
     }
     return;
   }
@@ -279,6 +314,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
   float acc[MB][4][2][4];
   uint32_t stage = 0;
   bool aborted = false;
+  bool epi_waited = !p.pdl;
 
   // Per-warp shared-memory offsets inside a stage, computed once: every
   // per-stage load is then (stage base + constant) with an immediate row
@@ -446,6 +482,12 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     }
 
     // ---------------------------------------------------------------- epilogue
+    // C, the split-K scratch and the workspace tickets may still be in use by
+    // the previous kernel on the stream until it has completed.
+    if (!epi_waited) {
+      grid_dependency_wait();
+      epi_waited = true;
+    }
     // 1) reduce the WPC warps of each chunk through shared memory, adding
     //    warp wk = 1, 2, ... to warp 0 in turn (fixed summation order; one
     //    slot per chunk keeps the smem for the ring).

@@ -30,6 +30,18 @@ namespace {
 
 thread_local std::string t_last_cuda_error;
 
+// Programmatic dependent launch between consecutive GEMM launches (on by
+// default; SM100_MARLIN_PDL=0 or sm100_marlin_set_overlap(0) turns it off).
+int g_pdl_override = -1;
+bool pdl_enabled() {
+  if (g_pdl_override >= 0) return g_pdl_override != 0;
+  static const bool env_on = [] {
+    const char* e = std::getenv("SM100_MARLIN_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return env_on;
+}
+
 // Device buffer for per-CTA timelines (only written by SM100_MARLIN_TRACE builds).
 unsigned long long* g_trace_buffer = nullptr;
 
@@ -248,8 +260,19 @@ int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
     if (e != cudaSuccess) return cuda_fail(e);
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaGetLastError();
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
@@ -356,6 +379,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.unit_kk = pl.unit_kk;
     p.units = pl.units;
     p.trace = g_trace_buffer;
+    p.pdl = pdl_enabled() ? 1 : 0;
     rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
     if (rc != SM100_MARLIN_OK) return rc;
     rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream) : dispatch<false>(p, pl, dev, stream);
@@ -484,6 +508,11 @@ const char* sm100_marlin_error_string(int code) {
 }
 
 const char* sm100_marlin_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
+
+int sm100_marlin_set_overlap(int enable) {
+  g_pdl_override = enable ? 1 : 0;
+  return SM100_MARLIN_OK;
+}
 
 int sm100_marlin_set_trace_buffer(void* buf) {
   g_trace_buffer = static_cast<unsigned long long*>(buf);

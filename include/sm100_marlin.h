@@ -117,6 +117,15 @@ const char* sm100_marlin_error_string(int code);
 /* Message of the last CUDA error seen by this library on this thread. */
 const char* sm100_marlin_last_cuda_error(void);
 
+/* Launch overlap between consecutive GEMM calls on one stream (programmatic
+ * dependent launch; on by default, or per SM100_MARLIN_PDL=0 in the
+ * environment).  With overlap on, a call may start streaming its WEIGHTS
+ * (B, meta, s) while the previous GEMM call on the stream is still running,
+ * so those buffers must not be written by that previous call; activations,
+ * C, workspace and scratch are only touched after it has completed.  No
+ * counterpart in the reference (whose launches never overlap). */
+int sm100_marlin_set_overlap(int enable);
+
 /* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 every GEMM
  * launch writes 8 uint64 words per CTA into `buf` (device memory, >= grid*64
  * bytes, zeroed by the caller): %globaltimer at kernel entry, first TMA issue,
