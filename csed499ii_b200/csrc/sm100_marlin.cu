@@ -26,6 +26,14 @@ namespace sm100 {
 
 __device__ int g_device_status = 0;
 
+// Split-K scratch of the allocation-free entry point
+// (sm100_marlin_mul_2_4_noalloc).  One copy per device that loads the
+// library, held until the process exits.  Every noalloc call on a device uses
+// the same bytes; the kernel writes each partial before any CTA reads it, so
+// nothing in it has to start at zero.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
 namespace {
 
 thread_local std::string t_last_cuda_error;
@@ -106,6 +114,24 @@ int get_scratch(int dev, cudaStream_t stream, size_t need, void** out) {
   if (e != cudaSuccess) return cuda_fail(e);
   slot = {p, bytes};
   *out = p;
+  return SM100_MARLIN_OK;
+}
+
+// Device address of g_noalloc_scratch on `dev` (the host-side symbol is only
+// a stand-in, never a device pointer).  Resolved once per device, with that
+// device current; the first noalloc call on a device does it.
+int noalloc_scratch(int dev, void** out) {
+  static std::mutex mu;
+  static void* ptr[64] = {};
+  if (dev < 0 || dev >= 64) return SM100_MARLIN_ERR_ARGUMENT;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    ptr[dev] = p;
+  }
+  *out = ptr[dev];
   return SM100_MARLIN_OK;
 }
 
@@ -418,6 +444,27 @@ int sm100_marlin_mul_2_4_ex(const void* A, const void* B, const void* meta, void
   if (scratch == nullptr) return SM100_MARLIN_ERR_SCRATCH;
   return mul_impl(A, B, meta, C, s, prob_m, prob_n, prob_k, workspace, groupsize, dev, stream,
                   thread_k, thread_m, sms, max_par, meta_bits, scratch, scratch_bytes);
+}
+
+int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta, void* C,
+                                 const void* s, int prob_m, int prob_n, int prob_k,
+                                 void* workspace, int groupsize, int dev, void* stream,
+                                 int thread_k, int thread_m, int sms, int max_par) {
+  int rc;
+  void* scratch = nullptr;
+  {
+    DeviceGuard guard(dev);
+    if (!guard.ok) return cuda_fail(cudaGetLastError());
+    rc = noalloc_scratch(dev, &scratch);
+  }
+  if (rc != SM100_MARLIN_OK) return rc;
+  rc = mul_impl(A, B, meta, C, s, prob_m, prob_n, prob_k, workspace, groupsize, dev, stream,
+                thread_k, thread_m, sms, max_par, 4, scratch, kNoAllocScratchBytes);
+  if (rc == SM100_MARLIN_ERR_SCRATCH)
+    t_last_cuda_error = "problem needs more split-K scratch than the " +
+                        std::to_string(kNoAllocScratchBytes >> 20) +
+                        " MiB static buffer of sm100_marlin_mul_2_4_noalloc";
+  return rc;
 }
 
 size_t sm100_marlin_scratch_bytes(int prob_m, int prob_n, int prob_k, int dev, int sms) {

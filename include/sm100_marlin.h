@@ -89,6 +89,29 @@ int sm100_marlin_mul_2_4_ex(const void* A, const void* B, const void* meta, void
                             int max_par, int meta_bits, void* scratch, size_t scratch_bytes);
 
 /*
+ * sm100_marlin_mul_2_4 without any device allocation.  No counterpart in the
+ * reference.  The regular entry point gets its split-K scratch from a cache
+ * it fills with cudaMalloc on first use; callers that may not allocate device
+ * memory at call time -- code running inside CUDA graph capture, serving
+ * runtimes and plugins whose host framework owns all device memory, or
+ * real-time loops that forbid allocation after start-up -- call this one
+ * instead.  Its scratch is a fixed 8 MiB static device buffer inside the
+ * library (one per device, kept until the process exits), enough for every
+ * call with prob_n (batch rows) <= 16 on up to 148 SMs.  Calls that need more
+ * return SM100_MARLIN_ERR_SCRATCH (see sm100_marlin_last_cuda_error).
+ * Arguments and results are those of sm100_marlin_mul_2_4.
+ * The first call on a device looks up the buffer's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All noalloc calls on a device share the buffer:
+ * calls that overlap on the GPU (different streams, no ordering between
+ * them) race and must be avoided; calls on one stream are safe.
+ */
+int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta, void* C,
+                                 const void* s, int prob_m, int prob_n, int prob_k,
+                                 void* workspace, int groupsize, int dev, void* stream,
+                                 int thread_k, int thread_m, int sms, int max_par);
+
+/*
  * 3-bit metadata codec.  Replaces `pack_metadata` / `unpack_metadata`
  * (kernel_experiments/sparse_marlin/metadata_decode/codec.cu:30-41).
  * pack:   meta int16[n_int16] (n_int16 % 128 == 0) -> out int32[n_int16*3/8];
