@@ -38,6 +38,10 @@ sys.path.insert(0, ROOT)
 LAYERS = 32
 SHAPES = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]  # (K, N)
 GROUP = 128
+# (batch rows, metadata bits) -> mean DRAM bytes per GEMM launch over SHAPES,
+# from ncu `dram__bytes_read.sum + dram__bytes_write.sum`
+# (profiles/marlin24_decode_llama7b_m16.md).
+MEASURED_TRAFFIC = {(16, 4): 19.994e6}
 
 
 def algo_bytes(M, K, N, meta_bits):
@@ -139,7 +143,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     layers = [[make_layer(torch, K, N, dev, gen, args.meta_bits) for (K, N) in SHAPES]
-              for _ in range(LAYERS)]
+              for _ in range(args.layers)]
     A = {K: torch.randn((M, K), dtype=torch.half, device=dev, generator=gen) for K in (4096, 11008)}
     C = {N: torch.empty((M, N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
     ws = torch.zeros(22016 // 128 * 16, dtype=torch.int32, device=dev)
@@ -155,8 +159,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
                 if rc != 0:
                     raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
 
-    bytes_step = LAYERS * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
-    launches_step = LAYERS * len(SHAPES) * ((M + 63) // 64)
+    bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
+    launches_step = args.layers * len(SHAPES) * ((M + 63) // 64)
 
     # warm-up eagerly (sizes the split-K scratch before capture), then capture
     with torch.cuda.stream(stream):
@@ -215,7 +219,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
                 g2.replay()
             ev1.record(stream)
         torch.cuda.synchronize(dev)
-        us = ev0.elapsed_time(ev1) * 1e3 / (reps * LAYERS)
+        us = ev0.elapsed_time(ev1) * 1e3 / (reps * args.layers)
         b = algo_bytes(M, K, N, args.meta_bits)
         detail[f"{K}x{N}"] = {"us": round(us, 3), "GB/s": round(b / us / 1e3, 1),
                               "TFLOP/s": round(2 * M * K * N / us / 1e6, 2)}
@@ -260,7 +264,11 @@ def bench_ours(args, torch, dist, rank, world, dev):
     d2h = sum(t.numel() * 2 for t in C_h.values())
 
     peak, peak_kind = load_peaks()
-    achieved = bytes_step / LAYERS / len(SHAPES) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
+    # DRAM bytes (read + write) per launch from one ncu capture of the same
+    # kernel and shapes (profiles/marlin24_decode_llama7b_m16.md), averaged
+    # over the four shapes like `achieved`; only known for the default case.
+    traffic = MEASURED_TRAFFIC.get((M, args.meta_bits))
+    achieved = bytes_step / args.layers / len(SHAPES) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
     return dict(
         value=value, ms_step=ms_step, per_launch_us=per_launch_us, bytes_step=bytes_step,
         launches=launches_step * args.steps, clocks=clk.summary(), detail=detail,
@@ -268,7 +276,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
                  d2h_bytes_per_step=d2h, steps=e2e_steps,
                  ms_per_step=round(e2e_ms / e2e_steps, 4)),
         roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s",
-                      frac=round(achieved / peak, 4), traffic=None,
+                      frac=round(achieved / peak, 4), traffic=traffic,
                       peak_source=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"),
     )
 
@@ -325,16 +333,19 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--meta-bits", type=int, choices=[3, 4], default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers per step (32 = Llama-2-7B; fewer only for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    config = {"workload": f"Llama-2-7B decode step: 32 layers x 4 GEMMs "
+    config = {"workload": f"Llama-2-7B decode step: {args.layers} layers x 4 GEMMs "
                           f"(K,N) in {SHAPES}, M={args.m}, 2:4 INT4 g128, {args.meta_bits}-bit meta",
               "model_shapes": "Llama-2-7B", "batch_rows": args.m, "groupsize": GROUP,
-              "meta_bits": args.meta_bits, "layers": LAYERS,
-              "l2": "inputs larger than L2: 32 distinct layers' weights (2.4 GB) per step",
+              "meta_bits": args.meta_bits, "layers": args.layers,
+              "l2": f"inputs larger than L2: {args.layers} distinct layers' weights "
+                    f"({args.layers * 75.4 / 1024:.2f} GB) per step",
               "parallelism": f"replicas x{args.gpus} (independent layers per GPU)"}
     metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-7B decode layer set, M={args.m})"
 
@@ -343,7 +354,7 @@ def main():
             return
         ref = cpu_reference(args.m, args.meta_bits, reps=max(args.steps, 1))
         line = dict(metric=metric, value=ref["value"], unit="GB/s", n_gpus=args.gpus,
-                    steps=args.steps, warmup=args.warmup, ms_per_step=round(ref["seconds_per_layer"] * LAYERS * 1e3, 3),
+                    steps=args.steps, warmup=args.warmup, ms_per_step=round(ref["seconds_per_layer"] * args.layers * 1e3, 3),
                     higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
                     data="synthetic", config=config, impl="reference",
                     cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
