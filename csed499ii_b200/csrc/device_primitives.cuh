@@ -18,8 +18,9 @@ namespace sm100 {
 // runs to completion without waiting any further.
 // ----------------------------------------------------------------------------
 enum : int {
-  kStatusFullWaitTimeout = 1,   // consumer waited too long for a stage
-  kStatusEmptyWaitTimeout = 2,  // producer waited too long for a free slot
+  kStatusFullWaitTimeout = 1,    // consumer waited too long for a stage
+  kStatusEmptyWaitTimeout = 2,   // producer waited too long for a free slot
+  kStatusFinishWaitTimeout = 4,  // split-K finisher waited too long for partials
 };
 
 // Upper bound for any single wait, in nanoseconds of %globaltimer.
@@ -86,6 +87,42 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   uint32_t polls = 0;
   while (!mbar_try_wait(bar, parity)) {
     if ((++polls & 1023u) != 0) continue;
+    if (*abort) return false;
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// GPU-scope counters for the split-K hand-over between CTAs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Fire-and-forget add (no return value, so the issuing thread does not wait
+// for the round trip).  Callers order their earlier writes with a fence.
+__device__ __forceinline__ void red_add_relaxed_gpu(int* p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Poll `*p` (acquire) until it reaches `target`.  Bounded like
+// mbar_wait_bounded: gives up (and raises `*abort`) after kWaitLimitNs, or
+// returns false when another thread raised `*abort`.
+__device__ __forceinline__ bool wait_counter_bounded(const int* p, int target,
+                                                     volatile int* abort) {
+  unsigned long long t0 = 0;
+  uint32_t polls = 0;
+  while (ld_acquire_gpu(p) < target) {
+    if ((++polls & 63u) != 0) continue;
     if (*abort) return false;
     const unsigned long long now = global_timer_ns();
     if (t0 == 0) {

@@ -27,10 +27,12 @@
 //    dequant with the group scale fused, and mma.sp m16n8k32 with fp32
 //    accumulators.
 //  * Split-K partials are reduced in fp32: warps of a CTA through shared
-//    memory, CTAs of a tile through a scratch buffer and a per-tile ticket in
-//    the caller's workspace; the last CTA to arrive sums all partials in CTA
-//    order with all its threads (deterministic; no CTA ever waits for another)
-//    and writes C.
+//    memory (a tree), CTAs of a tile through a scratch buffer and a per-tile
+//    counter in the caller's workspace.  The CTA holding a tile's first K
+//    units (for it always its last segment) finishes the tile: the others
+//    publish their partials and count them without waiting, a producer thread
+//    of the finisher polls the counter while its consumers still compute, and
+//    the finisher adds the partials in CTA order (deterministic) and writes C.
 #pragma once
 
 #include <cuda.h>
@@ -66,8 +68,9 @@ struct GemmParams {
 
 // Per-CTA timeline written when the library is built with
 // -DSM100_MARLIN_TRACE=1 (off by default): %globaltimer at kernel entry, first
-// TMA issue, first stage consumed, last stage consumed, end of epilogue, and
-// the number of stages and fixups of the CTA.
+// TMA issue, first stage consumed, last stage consumed, end of epilogue, the
+// number of stages and fixups of the CTA, and the time its consumers returned
+// from the programmatic-launch wait.
 constexpr int kTraceWords = 8;
 // CTA 0 additionally records per-stage SM clock cycles (clock64, cheap to
 // read) after the per-CTA words: [stage][0] producer issue, [1..3] consumer
@@ -75,6 +78,8 @@ constexpr int kTraceWords = 8;
 // consumer warp, [7] the CTA's clock at entry (for the offsets).
 constexpr int kTraceStages = 64;
 constexpr int kTraceStageWords = 8;
+// Words per launch in a trace buffer (grid <= 256 CTAs).
+constexpr long long kTraceLaunchWords = 256 * kTraceWords + kTraceStages * kTraceStageWords;
 #ifndef SM100_MARLIN_TRACE
 #define SM100_MARLIN_TRACE 0
 #endif
@@ -120,18 +125,24 @@ struct DecodeCfg {
   static constexpr int STAGE_RAW = OFF_S + S_ROWS * S_ROW;
   static constexpr int STAGE = (STAGE_RAW + 1023) / 1024 * 1024;
   static constexpr int ACC_F4 = 8 * MB;                          // float4 per thread of acc
-  static constexpr int RED_SLOTS = 1;                            // reduction slots per chunk
-  static constexpr int RED_BYTES = NC * RED_SLOTS * ACC_F4 * 32 * 16;
+  static constexpr int ACC_BYTES = ACC_F4 * 32 * 16;             // one warp's accumulators
   static constexpr int HEADER = 1024;                            // barriers + flags
+  // The warps sharing a chunk reduce pairwise (a tree); WPC/2 shared-memory
+  // slots per chunk let each level run in one pass, unless they would cost the
+  // ring more than one stage.
+  static constexpr int ring_depth(int slots) {
+    return (kSmemBudget - (HEADER + NC * slots * ACC_BYTES + 1023) / 1024 * 1024 - 1024) / STAGE;
+  }
+  static constexpr int RED_SLOTS =
+      (WPC / 2 > 1 && ring_depth(WPC / 2) + 1 >= ring_depth(1)) ? WPC / 2 : 1;
+  static constexpr int RED_BYTES = NC * RED_SLOTS * ACC_BYTES;
   static constexpr int RING_OFF = (HEADER + RED_BYTES + 1023) / 1024 * 1024;
   static constexpr int DEPTH_FIT = (kSmemBudget - RING_OFF - 1024) / STAGE;
-  static constexpr int DEPTH_RAW = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
-  static constexpr int DEPTH = DEPTH_RAW / PW * PW;              // slots per producer equal
+  static constexpr int DEPTH = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
   static constexpr int SMEM = RING_OFF + DEPTH * STAGE + 1024;   // +1024: base alignment slack
   static constexpr uint32_t STAGE_TX_NOSCALE = A_BOXES * A_BOX + SK * (B_ROW + M_ROW);
   static_assert(DEPTH >= PW, "ring too shallow for the producer warps");
   static constexpr uint32_t STAGE_TX_SCALE = STAGE_TX_NOSCALE + S_ROWS * S_ROW;
-  static constexpr int FIX_F4 = NC * ACC_F4;                     // float4 of a tile per lane
   static_assert(DEPTH >= 2, "ring too shallow");
   static_assert(SK % 4 == 0, "stage must hold whole scale groups");
   static_assert(!SCALE_ACC || RPW == 4, "accumulator scaling needs whole groups per warp");
@@ -159,23 +170,6 @@ __device__ __forceinline__ void fence_acq_rel_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
-__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
-  int old;
-  asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-
-// Element i (0..3) of float4 v of lane `lane` of a chunk's accumulator slot:
-// v = (mb*4 + j)*2 + h, element e -> (out-feature in chunk, batch row).
-__device__ __forceinline__ void acc_coords(int v, int lane, int e, int& n_in_chunk, int& row) {
-  const int h = v & 1;
-  const int j = (v >> 1) & 3;
-  const int mb = v >> 3;
-  const int g = lane >> 2, t = lane & 3;
-  n_in_chunk = 8 * g + j + 4 * (e >> 1);
-  row = 16 * mb + 8 * h + 2 * t + (e & 1);
-}
-
 template <int NC, int MB, int NH_LAST, bool META3, bool GROUPED>
 __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     marlin24_decode_kernel(const __grid_constant__ GemmParams p) {
@@ -192,7 +186,9 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty_bar = full_bar + D;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 512);
-  volatile int* ticket_sh = reinterpret_cast<volatile int*>(smem + 516);
+  // Split-K finisher hand-over: a producer thread arrives once the partials
+  // of every other CTA of the finisher's tile are published.
+  uint64_t* fin_bar = reinterpret_cast<uint64_t*>(smem + 520);
   uint8_t* red = smem + Cfg::HEADER;
   uint8_t* ring = smem + Cfg::RING_OFF;
 
@@ -210,7 +206,11 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     mbar_init(smem_addr(&empty_bar[threadIdx.x]), kConsumerWarps);
     fence_mbar_init();
   }
-  if (threadIdx.x == 0) *abort_flag = 0;
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(smem_addr(fin_bar), 1);
+    fence_mbar_init();
+  }
   // Let the next kernel on the stream start its prologue and weight prefetch
   // while this one runs (it waits for this grid before touching anything
   // this kernel reads or writes besides the weights).
@@ -240,11 +240,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       const uint64_t pol_keep = policy_evict_last();
       const uint32_t tx = GROUPED ? Cfg::STAGE_TX_SCALE : Cfg::STAGE_TX_NOSCALE;
       // With programmatic dependent launch the previous kernel on the stream
-      // may still be running: the weight parts of this warp's first stages
-      // (at most one ring's worth) are issued before griddepcontrol.wait; the
-      // activation parts, which the previous kernel may have produced, only
-      // after it.
-      constexpr int kPre = D / kProducerWarps;
+      // may still be running: the weight parts of the first ring's worth of
+      // stages are issued before griddepcontrol.wait; the activation parts,
+      // which the previous kernel may have produced, only after it.
+      constexpr int kPre = (D + kProducerWarps - 1) / kProducerWarps;
       int pre_slot[kPre], pre_kk[kPre];
       int n_pre = 0;
       bool waited = !p.pdl;
@@ -275,7 +274,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
           const uint32_t parity = ((stage / D) & 1u) ^ 1u;
           // a slot can only be free again after its stage was consumed, which
           // needs the deferred activation loads: release them first
-          if (!waited && n_pre == kPre) release_deferred();
+          if (!waited && static_cast<int>(stage) >= D) release_deferred();
           if (!mbar_wait_bounded(smem_addr(&empty_bar[slot]), parity, abort_flag)) {
             atomicOr(p.status, kStatusEmptyWaitTimeout);
             ok = false;
@@ -302,6 +301,22 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         }
       }
       if (!waited) release_deferred();
+      // Split-K finisher: when this CTA's last segment starts a tile that
+      // other CTAs finish, wait (here, while the consumers still compute) for
+      // their partials to be published, then hand over to the consumers.
+      // The counters are only read after griddepcontrol.wait (above), so the
+      // previous kernel's use of them is over.
+      if (pw == 0 && ok) {
+        const long long last_tile = (u_end - 1) / units_per_tile;
+        const long long t0 = last_tile * units_per_tile;
+        if (u_begin <= t0 && u_end < t0 + units_per_tile) {
+          const int others =
+              static_cast<int>(unit_owner(t0 + units_per_tile - 1, p.units, grid) - cta);
+          if (!wait_counter_bounded(&p.counters[last_tile], others, abort_flag))
+            atomicOr(p.status, kStatusFinishWaitTimeout);
+          mbar_arrive(smem_addr(fin_bar));
+        }
+      }
     }
     return;
   }
@@ -343,7 +358,6 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     const int ub = ui - tile * units_per_tile;
     const long long ue_ll = ub + (u_end - u);
     const int ue = ue_ll < units_per_tile ? static_cast<int>(ue_ll) : units_per_tile;
-    const bool first_seg = (u == u_begin);
     u += ue - ub;
     const int kb = ub * ukk, ke = ue * ukk;
 
@@ -487,34 +501,95 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     if (!epi_waited) {
       grid_dependency_wait();
       epi_waited = true;
+      if (trace && threadIdx.x == 0) trace[7] = global_timer_ns();
     }
-    // 1) reduce the WPC warps of each chunk through shared memory, adding
-    //    warp wk = 1, 2, ... to warp 0 in turn (fixed summation order; one
-    //    slot per chunk keeps the smem for the ring).
+    // 1) reduce the WPC warps of each chunk through shared memory as a tree:
+    //    at each level warps [h, 2h) add into warps [0, h) (slot-limited
+    //    passes); the summation order is fixed, so results are deterministic.
     float4* acc4 = reinterpret_cast<float4*>(&acc[0][0][0][0]);
     const int wk = warp / NC;  // warp index among the warps sharing this chunk
-    float4* red4 = reinterpret_cast<float4*>(red) + (cc * Cfg::ACC_F4) * 32;
-    for (int k2 = 1; k2 < Cfg::WPC; ++k2) {
-      if (wk == k2) {
+    for (int h = Cfg::WPC / 2; h >= 1; h /= 2) {
+      for (int base = 0; base < h; base += Cfg::RED_SLOTS) {
+        const int slot_w = wk - h - base;  // writer's slot this pass
+        const int slot_r = wk - base;      // reader's slot this pass
+        float4* red4w = reinterpret_cast<float4*>(red) +
+                        ((cc * Cfg::RED_SLOTS + slot_w) * Cfg::ACC_F4) * 32;
+        float4* red4r = reinterpret_cast<float4*>(red) +
+                        ((cc * Cfg::RED_SLOTS + slot_r) * Cfg::ACC_F4) * 32;
+        if (slot_w >= 0 && slot_w < Cfg::RED_SLOTS) {
 #pragma unroll
-        for (int v = 0; v < Cfg::ACC_F4; ++v) red4[v * 32 + lane] = acc4[v];
-      }
-      named_bar_sync(1, kConsumerWarps * 32);
-      if (wk == 0) {
-#pragma unroll
-        for (int v = 0; v < Cfg::ACC_F4; ++v) {
-          const float4 x = red4[v * 32 + lane];
-          acc4[v].x += x.x; acc4[v].y += x.y; acc4[v].z += x.z; acc4[v].w += x.w;
+          for (int v = 0; v < Cfg::ACC_F4; ++v) red4w[v * 32 + lane] = acc4[v];
         }
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (slot_r >= 0 && slot_r < Cfg::RED_SLOTS) {
+#pragma unroll
+          for (int v = 0; v < Cfg::ACC_F4; ++v) {
+            const float4 x = red4r[v * 32 + lane];
+            acc4[v].x += x.x; acc4[v].y += x.y; acc4[v].z += x.z; acc4[v].w += x.w;
+          }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
       }
-      named_bar_sync(1, kConsumerWarps * 32);
     }
 
     const bool complete = (kb == 0 && ke == p.kk_total);
-    if (complete) {
-      if (wk != 0) continue;
-      // 2a) the whole K range of the tile was reduced here: the leader warp of
-      //     each chunk converts and stores 16-byte rows of C.
+    if (!complete && kb != 0) {
+      // 2a) contributor: this segment ends a tile that another CTA (the one
+      //     holding the tile's first K units) finishes.  Publish the partial
+      //     in this CTA's scratch slot and count it; nobody waits here.
+      //     (Such a segment is always the CTA's first.)
+      if (wk == 0) {
+        float4* part = p.partials + ((cta * NC + cc) * Cfg::ACC_F4) * 32;
+#pragma unroll
+        for (int v = 0; v < Cfg::ACC_F4; ++v) part[v * 32 + lane] = acc4[v];
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+      if (threadIdx.x == 0) {
+        fence_acq_rel_gpu();
+        red_add_relaxed_gpu(&p.counters[tile], 1);
+      }
+      continue;
+    }
+    if (wk != 0) continue;
+    if (!complete) {
+      // 2b) finisher (always the CTA's last segment): a producer thread has
+      //     waited for the other CTAs' partials; add them in CTA order.
+      if (aborted || !mbar_wait_bounded(smem_addr(fin_bar), 0, abort_flag) || *abort_flag) {
+        if (!aborted && lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
+        continue;
+      }
+      if (trace && threadIdx.x == 0) trace[6] += 1;
+      const long long t0 = static_cast<long long>(tile) * units_per_tile;
+      const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
+      // two contributors' loads in flight at a time, 8 float4 per lane each
+      constexpr int VB = Cfg::ACC_F4 < 8 ? Cfg::ACC_F4 : 8;
+      for (long long c = cta + 1; c <= c_hi; c += 2) {
+        const bool two = c + 1 <= c_hi;
+        const float4* src0 = p.partials + ((c * NC + cc) * Cfg::ACC_F4) * 32 + lane;
+        const float4* src1 = two ? src0 + NC * Cfg::ACC_F4 * 32 : src0;
+#pragma unroll
+        for (int vb = 0; vb < Cfg::ACC_F4; vb += VB) {
+          float4 x0[VB], x1[VB];
+#pragma unroll
+          for (int v = 0; v < VB; ++v) {
+            x0[v] = __ldcg(src0 + (vb + v) * 32);
+            x1[v] = two ? __ldcg(src1 + (vb + v) * 32) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int v = 0; v < VB; ++v) {
+            float4& a = acc4[vb + v];
+            a.x += x0[v].x; a.y += x0[v].y; a.z += x0[v].z; a.w += x0[v].w;
+            if (two) {
+              a.x += x1[v].x; a.y += x1[v].y; a.z += x1[v].z; a.w += x1[v].w;
+            }
+          }
+        }
+      }
+      // every contribution has arrived and been counted: re-arm the counter
+      if (cc == 0 && lane == 0) p.counters[tile] = 0;
+    }
+    // 3) the leader warp of each chunk converts and stores 16-byte rows of C.
+    {
       const int n0 = (tile * NC + cc) * 64 + 8 * g;
       float colscale[8];
       if (!GROUPED) {
@@ -550,79 +625,6 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
             for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
             *reinterpret_cast<uint4*>(p.C + static_cast<long long>(r) * p.N + n0) = o;
           }
-      continue;
-    }
-
-    // 2b) partial K range: publish this CTA's partial, take a ticket; the last
-    //     CTA of the tile sums every partial in CTA order.
-    const long long my_slot = 2 * cta + (first_seg ? 0 : 1);
-    if (wk == 0) {
-      float4* part = p.partials + ((my_slot * NC + cc) * Cfg::ACC_F4) * 32;
-#pragma unroll
-      for (int v = 0; v < Cfg::ACC_F4; ++v) part[v * 32 + lane] = acc4[v];
-    }
-    named_bar_sync(1, kConsumerWarps * 32);
-    const long long t0 = static_cast<long long>(tile) * units_per_tile;
-    const long long c_lo = unit_owner(t0, p.units, grid);
-    const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
-    if (threadIdx.x == 0) {
-      fence_acq_rel_gpu();
-      const int prev = atomic_add_acq_rel(&p.counters[tile], 1);
-      *ticket_sh = (prev == static_cast<int>(c_hi - c_lo)) ? 1 : 0;
-    }
-    named_bar_sync(1, kConsumerWarps * 32);
-    if (*ticket_sh == 0) continue;
-    if (trace && threadIdx.x == 0) trace[6] += 1;
-    fence_acq_rel_gpu();
-    // thread i handles float4 positions i, i + 256, ... of the tile's NC slots
-    constexpr int PER = (Cfg::FIX_F4 * 32 + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
-    float4 sum[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) sum[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    // two participants' loads in flight at a time; summed in CTA order
-    for (long long c = c_lo; c <= c_hi; c += 2) {
-      const bool two = c + 1 <= c_hi;
-      const float4* src0 =
-          p.partials + ((2 * c + (unit_begin(c, p.units, grid) >= t0 ? 0 : 1)) * NC) * Cfg::ACC_F4 * 32;
-      const float4* src1 =
-          two ? p.partials + ((2 * (c + 1) + (unit_begin(c + 1, p.units, grid) >= t0 ? 0 : 1)) * NC) *
-                                 Cfg::ACC_F4 * 32
-              : src0;
-      float4 x0[PER], x1[PER];
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int pos = threadIdx.x + i * kConsumerWarps * 32;
-        const bool in = pos < Cfg::FIX_F4 * 32;
-        x0[i] = in ? __ldcg(src0 + pos) : make_float4(0.f, 0.f, 0.f, 0.f);
-        x1[i] = (in && two) ? __ldcg(src1 + pos) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        sum[i].x += x0[i].x; sum[i].y += x0[i].y; sum[i].z += x0[i].z; sum[i].w += x0[i].w;
-        if (two) {
-          sum[i].x += x1[i].x; sum[i].y += x1[i].y; sum[i].z += x1[i].z; sum[i].w += x1[i].w;
-        }
-      }
-    }
-    if (threadIdx.x == 0) p.counters[tile] = 0;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int pos = threadIdx.x + i * kConsumerWarps * 32;
-      if (pos >= Cfg::FIX_F4 * 32) continue;
-      const int ch = pos / (Cfg::ACC_F4 * 32);
-      const int v = (pos / 32) % Cfg::ACC_F4;
-      const int ln = pos % 32;
-      const float vals[4] = {sum[i].x, sum[i].y, sum[i].z, sum[i].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int nc, row;
-        acc_coords(v, ln, e, nc, row);
-        if (row >= p.M) continue;
-        const int n = (tile * NC + ch) * 64 + nc;
-        float val = vals[e];
-        if (!GROUPED) val *= __half2float(reinterpret_cast<const half*>(p.s)[n]);
-        p.C[static_cast<long long>(row) * p.N + n] = __float2half_rn(val);
-      }
     }
   }
   if (trace && threadIdx.x == 0) trace[4] = global_timer_ns();

@@ -52,6 +52,8 @@ bool pdl_enabled() {
 
 // Device buffer for per-CTA timelines (only written by SM100_MARLIN_TRACE builds).
 unsigned long long* g_trace_buffer = nullptr;
+// Trace builds: launch k writes its records at g_trace_buffer + k * kTraceLaunchWords.
+long long g_trace_launch = 0;
 
 int cuda_fail(cudaError_t e) {
   t_last_cuda_error = cudaGetErrorString(e);
@@ -186,7 +188,8 @@ Plan make_plan(int n_out, int m_rows, int k_in, int sms) {
   const long long n_tiles = n_out / (64 * pl.nc);
   pl.units = n_tiles * (kk / pl.unit_kk);
   pl.grid = static_cast<int>(pl.units < sms ? pl.units : sms);
-  pl.scratch = static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 8192;
+  // one fp32 partial tile (nc chunks x 16*mb rows x 64 columns) per CTA
+  pl.scratch = static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 4096;
   return pl;
 }
 
@@ -404,7 +407,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.kk_total = prob_k / 32;
     p.unit_kk = pl.unit_kk;
     p.units = pl.units;
-    p.trace = g_trace_buffer;
+    p.trace = g_trace_buffer ? g_trace_buffer + g_trace_launch++ * kTraceLaunchWords : nullptr;
     p.pdl = pdl_enabled() ? 1 : 0;
     rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
     if (rc != SM100_MARLIN_OK) return rc;
@@ -563,6 +566,7 @@ int sm100_marlin_set_overlap(int enable) {
 
 int sm100_marlin_set_trace_buffer(void* buf) {
   g_trace_buffer = static_cast<unsigned long long*>(buf);
+  g_trace_launch = 0;
   return SM100_MARLIN_TRACE ? SM100_MARLIN_OK : SM100_MARLIN_ERR_ARGUMENT;
 }
 

@@ -34,6 +34,7 @@ extern "C" {
 /* Bits of the device status word (sm100_marlin_device_status). */
 #define SM100_MARLIN_STATUS_FULL_WAIT_TIMEOUT 1
 #define SM100_MARLIN_STATUS_EMPTY_WAIT_TIMEOUT 2
+#define SM100_MARLIN_STATUS_FINISH_WAIT_TIMEOUT 4
 
 /*
  * C[prob_n, prob_m] (fp16, row-major) = A[prob_n, prob_k] (fp16, row-major)
@@ -149,10 +150,12 @@ const char* sm100_marlin_last_cuda_error(void);
  * counterpart in the reference (whose launches never overlap). */
 int sm100_marlin_set_overlap(int enable);
 
-/* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 every GEMM
- * launch writes 8 uint64 words per CTA into `buf` (device memory, >= grid*64
- * bytes, zeroed by the caller): %globaltimer at kernel entry, first TMA issue,
- * first and last stage consumed, end of the CTA, stage count, fixup count.
+/* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 the k-th
+ * GEMM launch after this call writes into `buf` (device memory, zeroed by the
+ * caller, 20 KiB per launch) at offset k * 20 KiB: per CTA 8 uint64 words
+ * (%globaltimer at kernel entry, first TMA issue, first and last stage
+ * consumed, end of the CTA, stage count, fixup count, return from the
+ * programmatic-launch wait), then per-stage clock64 stamps of CTA 0.
  * Returns SM100_MARLIN_ERR_ARGUMENT in normal builds (nothing is recorded).
  * No counterpart in the reference (its profiling is external, via ncu). */
 int sm100_marlin_set_trace_buffer(void* buf);
