@@ -94,11 +94,12 @@ constexpr int producer_warps(int nc, int mb) { return (mb == 1 || (nc == 1 && mb
 constexpr int rows_per_warp(int nc, int mb) {
   return mb == 1 ? 4 : (((nc == 1 && mb > 1) || (nc == 2 && mb == 4)) ? 1 : 2);
 }
-// With one 16-row batch block a warp owns a whole 128-K scale group per
-// stage: its four row products go to a temporary fp32 accumulator that is
-// scaled once per group (instead of scaling every dequantised weight in
-// fp16).  Measured faster than per-weight scaling in the full kernel.
-constexpr bool scale_on_accumulator(int mb) { return mb == 1; }
+// Group scales are applied to the dequantised weights (fp16 multiply, as the
+// reference does) rather than to per-group fp32 temporaries: on B200 the
+// temporaries' extra accumulator traffic costs more than the multiplies
+// (118 vs 69 cycles per 32x64 block per sub-partition, measured).  The
+// accumulator variant stays available for experiments.
+constexpr bool scale_on_accumulator(int mb) { return false; }
 
 constexpr int kSmemBudget = 227 * 1024;
 
@@ -334,8 +335,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
   // Per-warp shared-memory offsets inside a stage, computed once: every
   // per-stage load is then (stage base + constant) with an immediate row
   // offset.  Activations: row ar of the 128B-swizzled box keeps 16-byte chunk
-  // c at chunk c ^ (ar & 7); a_off[p][mb][i] is the chunk holding K 16i..16i+7
-  // (lanes 0-15) / 16i+8..16i+15 (lanes 16-31) of a row with parity p.
+  // c at chunk c ^ (ar & 7).  a_off[p][mb][h] addresses, for a 32-K row of
+  // parity p, the 8 batch rows 16mb+8h.. with lane group q = lane/8 on K
+  // 8q..8q+7, so one ldmatrix.x4 returns a complete mma B operand in order
+  // (assembling it from two loads costs ~30 % of the inner loop).
   const uint32_t b_off = Cfg::OFF_B + kl * Cfg::B_ROW + cc * 512 + lane * 16;
   const uint32_t m_off = Cfg::OFF_M + kl * Cfg::M_ROW + cc * Cfg::M_BLK +
                          (META3 ? lane * 4 : (lane & 15) * 16);
@@ -344,13 +347,13 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
 #pragma unroll
   for (int par = 0; par < 2; ++par)
 #pragma unroll
-    for (int mb = 0; mb < MB; ++mb) {
-      const int ar = 16 * mb + (lane & 15);
-      const int c0 = par * 4 + (lane >> 4);
-      a_off[par][mb][0] = Cfg::OFF_A + (kl >> 1) * Cfg::A_BOX + ar * 128 + ((c0 ^ (ar & 7)) << 4);
-      a_off[par][mb][1] =
-          Cfg::OFF_A + (kl >> 1) * Cfg::A_BOX + ar * 128 + (((c0 + 2) ^ (ar & 7)) << 4);
-    }
+    for (int mb = 0; mb < MB; ++mb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int ar = 16 * mb + 8 * h + (lane & 7);
+        const int c = par * 4 + (lane >> 3);
+        a_off[par][mb][h] = Cfg::OFF_A + (kl >> 1) * Cfg::A_BOX + ar * 128 + ((c ^ (ar & 7)) << 4);
+      }
 
   for (long long u = u_begin; u < u_end;) {
     const int ui = static_cast<int>(u);
@@ -414,13 +417,12 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
             const uint32_t abox = st + (((kl & 1) + r) >> 1) * Cfg::A_BOX;
             uint32_t bf[MB][2][4];
 #pragma unroll
-            for (int mb = 0; mb < MB; ++mb) {
-              uint32_t r0[4], r1[4];
-              ldmatrix_x4(r0, abox + (par ? a_off[1][mb][0] : a_off[0][mb][0]));
-              ldmatrix_x4(r1, abox + (par ? a_off[1][mb][1] : a_off[0][mb][1]));
-              bf[mb][0][0] = r0[0]; bf[mb][0][1] = r0[2]; bf[mb][0][2] = r1[0]; bf[mb][0][3] = r1[2];
-              bf[mb][1][0] = r0[1]; bf[mb][1][1] = r0[3]; bf[mb][1][2] = r1[1]; bf[mb][1][3] = r1[3];
-            }
+            for (int mb = 0; mb < MB; ++mb)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (h == 1 && mb == MB - 1 && NH_LAST == 1) continue;
+                ldmatrix_x4(bf[mb][h], abox + (par ? a_off[1][mb][h] : a_off[0][mb][h]));
+              }
             const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
