@@ -64,6 +64,7 @@ struct GemmParams {
   long long units;      // n_tiles * kk_total / unit_kk
   unsigned long long* trace;  // optional per-CTA timestamps (SM100_MARLIN_TRACE builds)
   int pdl;              // launched with programmatic dependent launch
+  int prefetch;         // stages whose weights may be issued before griddepcontrol.wait
 };
 
 // Per-CTA timeline written when the library is built with
@@ -275,7 +276,8 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
           const uint32_t parity = ((stage / D) & 1u) ^ 1u;
           // a slot can only be free again after its stage was consumed, which
           // needs the deferred activation loads: release them first
-          if (!waited && static_cast<int>(stage) >= D) release_deferred();
+          if (!waited && static_cast<int>(stage) >= (p.prefetch < D ? p.prefetch : D))
+            release_deferred();
           if (!mbar_wait_bounded(smem_addr(&empty_bar[slot]), parity, abort_flag)) {
             atomicOr(p.status, kStatusEmptyWaitTimeout);
             ok = false;

@@ -50,6 +50,17 @@ bool pdl_enabled() {
   return env_on;
 }
 
+// Stages whose weights a kernel may stream before the previous kernel on the
+// stream has completed (default: the whole ring).  SM100_MARLIN_PREFETCH=n
+// caps it (tuning knob).
+int prefetch_stages() {
+  static const int v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFETCH");
+    return e ? std::atoi(e) : (1 << 30);
+  }();
+  return v;
+}
+
 // Device buffer for per-CTA timelines (only written by SM100_MARLIN_TRACE builds).
 unsigned long long* g_trace_buffer = nullptr;
 // Trace builds: launch k writes its records at g_trace_buffer + k * kTraceLaunchWords.
@@ -409,6 +420,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.units = pl.units;
     p.trace = g_trace_buffer ? g_trace_buffer + g_trace_launch++ * kTraceLaunchWords : nullptr;
     p.pdl = pdl_enabled() ? 1 : 0;
+    p.prefetch = prefetch_stages();
     rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
     if (rc != SM100_MARLIN_OK) return rc;
     rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream) : dispatch<false>(p, pl, dev, stream);
