@@ -137,6 +137,7 @@ def make_layer(torch, K, N, dev, gen, meta_bits):
 def bench_ours(args, torch, dist, rank, world, dev):
     import csed499ii_b200 as m
     from csed499ii_b200 import metadata_decode as md
+    from csed499ii_b200 import shard
 
     lib = m._ext.load()
     M = args.m
@@ -146,6 +147,13 @@ def bench_ours(args, torch, dist, rank, world, dev):
               for _ in range(args.layers)]
     A = {K: torch.randn((M, K), dtype=torch.half, device=dev, generator=gen) for K in (4096, 11008)}
     C = {N: torch.empty((M, N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
+    # N > 1: column-parallel layers of width world * N; this rank holds one
+    # N-wide shard and every GEMM is followed by the all-gather of C
+    Cg = {N: torch.empty((M, world * N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
+
+    def gather(N):
+        if world > 1:
+            shard.gather_columns(C[N], out=Cg[N])
     ws = torch.zeros(22016 // 128 * 16, dtype=torch.int32, device=dev)
     devi = dev.index
     fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
@@ -158,6 +166,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
                         N, M, K, ws.data_ptr(), GROUP // 2, devi, s_ptr, -1, -1, -1, 16)
                 if rc != 0:
                     raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
+                gather(N)
 
     bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
     launches_step = args.layers * len(SHAPES) * ((M + 63) // 64)
@@ -209,6 +218,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
                 B, meta, s = lay[idx]
                 fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(), s.data_ptr(),
                    N, M, K, ws.data_ptr(), GROUP // 2, devi, sp, -1, -1, -1, 16)
+                gather(N)
         for _ in range(3):
             g2.replay()
         torch.cuda.synchronize(dev)
@@ -227,7 +237,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
 
     # ---- end to end through the public operator, host buffers
     A_h = {K: A[K].cpu().pin_memory() for K in A}
-    C_h = {N: torch.empty((M, N), dtype=torch.half).pin_memory() for N in C}
+    C_h = {N: torch.empty((M, world * N), dtype=torch.half).pin_memory() for N in C}
+    C_out = Cg if world > 1 else C
     A_d = {K: torch.empty_like(A[K]) for K in A}
     e2e_steps = max(3, min(args.steps, 20))
 
@@ -240,8 +251,9 @@ def bench_ours(args, torch, dist, rank, world, dev):
                     m.mul_2_4(A_d[K], B, meta, C[N], s, ws)
                 else:
                     md.matmul(A_d[K], B, meta, C[N], s, ws)
+                gather(N)
         for N in C_h:
-            C_h[N].copy_(C[N], non_blocking=True)
+            C_h[N].copy_(C_out[N], non_blocking=True)
 
     with torch.cuda.stream(stream):
         for _ in range(2):
@@ -346,7 +358,10 @@ def main():
               "meta_bits": args.meta_bits, "layers": args.layers,
               "l2": f"inputs larger than L2: {args.layers} distinct layers' weights "
                     f"({args.layers * 75.4 / 1024:.2f} GB) per step",
-              "parallelism": f"replicas x{args.gpus} (independent layers per GPU)"}
+              "parallelism": ("single GPU" if args.gpus == 1 else
+                              f"tp{args.gpus} column-parallel: each rank holds an N-wide shard of "
+                              f"{args.gpus}N-wide layers (weak scaling), NCCL all-gather of C after "
+                              f"every GEMM")}
     metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-7B decode layer set, M={args.m})"
 
     if args.impl == "reference":

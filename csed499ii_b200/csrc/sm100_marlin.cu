@@ -154,9 +154,11 @@ int device_sms(int dev, int* sms) {
 }
 
 // Column-tile width (in 64-column chunks).  Wider tiles re-read the
-// activations less often; narrower tiles leave fewer CTAs sharing one tile,
-// which bounds the split-K fixup (its cost grows with the CTAs per tile).
-// Picks the widest tile with at most four CTAs per tile.
+// activations less often, but when there are fewer tiles than CTAs some CTA
+// works entirely inside one tile and finishes at the same time as the CTA
+// that completes the tile, which puts the split-K hand-over on the critical
+// path.  So: the widest tile that still gives every CTA at least one tile
+// boundary, else one chunk (measured best for every Llama-2-7B shape).
 // SM100_MARLIN_NC=1|2|4 overrides (tuning knob).
 int choose_nc(int n_out, int sms) {
   static const int forced = [] {
@@ -165,12 +167,8 @@ int choose_nc(int n_out, int sms) {
   }();
   const int chunks = n_out / 64;
   if ((forced == 1 || forced == 2 || forced == 4) && chunks % forced == 0) return forced;
-  for (int nc : {4, 2}) {
-    if (chunks % nc) continue;
-    const int tiles = chunks / nc;
-    const int per_tile = (sms + tiles - 1) / tiles;
-    if (per_tile <= 4) return nc;
-  }
+  for (int nc : {4, 2})
+    if (chunks % nc == 0 && chunks / nc >= sms) return nc;
   return 1;
 }
 

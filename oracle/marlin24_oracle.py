@@ -34,7 +34,7 @@ reference packer by the golden tests):
   code of the kept value at out-feature ``n = 64cc + 8g + j + 4*((i>>1)&1)``
   and compressed column ``kc = 16kk + 8*(i&1) + 2t + (i>>2)``.
 * ``meta``: int16 ``(N, K/16)`` storage, read as flat int32 words.  Word
-  ``kk*(N/2) + 64*cc + w`` (``w = 32c + 4a + 2d + h``) holds in its low half
+  ``kk*N + 64*cc + w`` (``w = 32c + 4a + 2d + h``) holds in its low half
   the 4 nibbles of out-feature ``n = 64cc + 8a + 2c + d`` for dense k in
   ``[32kk + 16h, 32kk + 16h + 16)`` and in its high half those of ``n + 4``.
   Nibble = ``idx0 | idx1 << 2`` (positions of the two kept values).

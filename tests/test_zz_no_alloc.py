@@ -61,8 +61,9 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     from csed499ii_b200 import _ext
 
     lib = _ext.load()
-    # 64 batch rows on a wide layer need more than the static 8 MiB of scratch
-    N, K, M = 22016, 4096, 64
+    # 64 batch rows on a very wide layer (Llama-2-70B gate+up) need more than
+    # the static 8 MiB of scratch
+    N, K, M = 57344, 1024, 64
     A = torch.zeros((M, K), dtype=torch.half, device=DEV)
     C = torch.zeros((M, N), dtype=torch.half, device=DEV)
     B = torch.zeros((K // 32, 2 * N), dtype=torch.int32, device=DEV)
