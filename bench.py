@@ -336,6 +336,52 @@ def cpu_reference(M, meta_bits, reps, layers_sample=1, budget_s=25.0):
                 seconds_per_layer=t)
 
 
+PREFILL_SHAPES = [(4096, 4096), (8192, 8192), (4096, 11008)]  # (K, N)
+PREFILL_M = [512, 2048, 8192]
+
+
+def bench_prefill(args, torch, dev):
+    """Compute-bound regime: dense-equivalent TFLOP/s of single GEMMs."""
+    import csed499ii_b200 as m
+
+    lib = m._ext.load()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321)
+    devi = dev.index
+    detail, flops_total, sec_total = {}, 0.0, 0.0
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.Stream(device=dev)
+    for (K, N) in PREFILL_SHAPES:
+        B, meta, s = make_layer(torch, K, N, dev, gen, 4)
+        ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
+        for M in PREFILL_M:
+            A = torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
+            C = torch.empty((M, N), dtype=torch.half, device=dev)
+
+            def call():
+                rc = lib.sm100_marlin_mul_2_4(A.data_ptr(), B.data_ptr(), meta.data_ptr(),
+                                              C.data_ptr(), s.data_ptr(), N, M, K, ws.data_ptr(),
+                                              GROUP // 2, devi, stream.cuda_stream, -1, -1, -1, 16)
+                if rc != 0:
+                    raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
+            for _ in range(args.warmup):
+                call()
+            torch.cuda.synchronize(dev)
+            reps = max(3, min(args.steps, 20))
+            with torch.cuda.stream(stream):
+                ev0.record(stream)
+                for _ in range(reps):
+                    call()
+                ev1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = ev0.elapsed_time(ev1) * 1e-3 / reps
+            fl = 2.0 * M * N * K
+            detail[f"M{M}_K{K}_N{N}"] = {"us": round(t * 1e6, 1), "TFLOP/s": round(fl / t / 1e12, 1)}
+            flops_total += fl
+            sec_total += t
+    return flops_total / sec_total / 1e12, detail
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -345,6 +391,9 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--meta-bits", type=int, choices=[3, 4], default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: Llama-2-7B decode step (config 1, the headline); "
+                         "prefill: compute-bound sweep (config 4)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers per step (32 = Llama-2-7B; fewer only for profiling)")
     args = ap.parse_args()
@@ -394,6 +443,26 @@ def main():
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
 
+    if args.workload == "prefill":
+        value, detail = bench_prefill(args, torch, dev)
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                dense = float(json.load(f)["bf16_tflops"])
+            kind = "derived: 2 x measured dense bf16 (MEASURED_PEAKS.json)"
+        except Exception:
+            dense, kind = 1590.0, "derived: 2 x fallback dense"
+        line = dict(metric="2:4 W4A16 GEMM dense-equivalent TFLOP/s (prefill sweep, config 4)",
+                    value=round(value, 1), unit="TFLOP/s", n_gpus=1, steps=args.steps,
+                    warmup=args.warmup, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="f16", data="synthetic (random packed INT4 codes, legal 2:4 metadata)",
+                    config={"workload": f"M in {PREFILL_M} x (K,N) in {PREFILL_SHAPES}, g128"},
+                    roofline={"bound": "tensor", "achieved": round(value, 1), "peak": 2 * dense,
+                              "unit": "TFLOP/s", "frac": round(value / (2 * dense), 4),
+                              "peak_source": kind},
+                    detail=detail)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     res = bench_ours(args, torch, dist, rank, world, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

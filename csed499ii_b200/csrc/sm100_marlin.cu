@@ -20,6 +20,7 @@
 #include "../../include/sm100_marlin.h"
 #include "device_primitives.cuh"
 #include "marlin24_gemm.cuh"
+#include "marlin24_prefill.cuh"
 #include "meta3_codec.cuh"
 
 namespace sm100 {
@@ -363,6 +364,73 @@ int check_reference_shape(int prob_m, int prob_n, int prob_k, int groupsize, int
   return SM100_MARLIN_OK;
 }
 
+// Batches above this many rows go to the tensor-memory (tcgen05) kernel in
+// one launch instead of 64-row decode launches.  SM100_MARLIN_PREFILL_MIN=n
+// changes it (tuning knob; a very large value disables the prefill kernel).
+int prefill_min_rows() {
+  static const int v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_MIN");
+    return e ? std::atoi(e) : 64;
+  }();
+  return v;
+}
+
+template <int BN, bool GROUPED>
+int launch_prefill_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
+  using Cfg = PrefillCfg<BN>;
+  static bool attr_set[64] = {};
+  auto kern = marlin24_prefill_kernel<BN, GROUPED>;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const dim3 grid(p.N / 128, (p.M + BN - 1) / BN);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+// C[M, N] = A . dequant(B, meta, s) for M > prefill_min_rows() (4-bit
+// metadata): one 128 x BN output tile per CTA on the tcgen05 kernel.
+int mul_prefill(const void* A, const void* B, const void* meta, void* C, const void* s, int n_out,
+                int m_rows, int k_in, int groupsize, int dev, int sms, cudaStream_t stream,
+                int* status) {
+  PrefillParams p;
+  p.s = static_cast<const uint8_t*>(s);
+  p.C = static_cast<half*>(C);
+  p.status = status;
+  p.M = m_rows;
+  p.N = n_out;
+  p.K = k_in;
+  p.grouped = groupsize != -1 ? 1 : 0;
+  const int n_tiles = n_out / 128;
+  const int bn = (m_rows >= 256 && static_cast<long long>(n_tiles) * ((m_rows + 255) / 256) >= sms)
+                     ? 256 : 128;
+  const uint64_t N = n_out, K = k_in;
+  int rc = encode_2d(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, static_cast<uint64_t>(m_rows),
+                     2 * K, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 2,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 2,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (p.grouped) {
+    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    std::memset(&p.tm_s, 0, sizeof(p.tm_s));
+  }
+  if (bn == 256)
+    return p.grouped ? launch_prefill_cfg<256, true>(p, dev, stream)
+                     : launch_prefill_cfg<256, false>(p, dev, stream);
+  return p.grouped ? launch_prefill_cfg<128, true>(p, dev, stream)
+                   : launch_prefill_cfg<128, false>(p, dev, stream);
+}
+
 int mul_impl(const void* A, const void* B, const void* meta, void* C, const void* s, int prob_m,
              int prob_n, int prob_k, void* workspace, int groupsize, int dev, void* stream_v,
              int thread_k, int thread_m, int sms, int max_par, int meta_bits, void* scratch,
@@ -386,6 +454,14 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     if (rc != SM100_MARLIN_OK) return rc;
   }
   if (sms <= 0) return SM100_MARLIN_ERR_ARGUMENT;
+
+  if (meta_bits == 4 && prob_n > prefill_min_rows() && prob_m % 128 == 0 && prob_k % 64 == 0) {
+    int* status = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return mul_prefill(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
+                       status);
+  }
 
   const int chunk_rows = prob_n < 64 ? prob_n : 64;
   Plan big = make_plan(prob_m, chunk_rows, prob_k, sms);

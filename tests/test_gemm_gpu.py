@@ -170,3 +170,29 @@ def test_reference_error_messages():
         m.mul_2_4(A, B, meta, C, s, ws)
     with pytest.raises(RuntimeError, match="No kernel implementation for thread_k=128"):
         m.mul_2_4(A, B, meta, C[:, :256].contiguous(), s[:, :256].contiguous(), ws, 128, 128)
+
+
+# Batches above 64 rows run on the tensor-memory (tcgen05) kernel in one
+# launch: BASELINE config-4 shapes at the small end of its batch range,
+# ragged batch tiles, both scale modes, and K not a multiple of 128.
+@pytest.mark.parametrize("K,N,M", [(4096, 4096, 512), (4096, 11008, 512), (4096, 4096, 2048),
+                                   (1024, 512, 300), (2048, 768, 1000), (4096, 4096, 257)])
+def test_prefill_shapes(K, N, M):
+    W, B, s, meta = random_packed_problem(N, K, 128, seed=K + M)
+    A = activations(M, K, seed=M)
+    check(run(A, B, meta, s, N), oracle_c(A, W))
+
+
+@pytest.mark.parametrize("K", [512, 704])
+def test_prefill_per_column_scales(K):
+    W, B, s, meta = quantized_problem(512, K, -1, seed=9)
+    A = activations(160, K, seed=10)
+    check(run(A, B, meta, s, 512, 64, 256), oracle_c(A, W))
+
+
+def test_prefill_deterministic():
+    W, B, s, meta = random_packed_problem(1024, 2048, 128, seed=12)
+    A = activations(384, 2048, seed=13)
+    C0 = run(A, B, meta, s, 1024)
+    for _ in range(3):
+        assert torch.equal(run(A, B, meta, s, 1024), C0)
