@@ -14,7 +14,8 @@
 //    (TMA, 128-byte swizzle: already the UMMA K-major canonical layout) and
 //    the packed weights, metadata and scales of the 128 output features into
 //    a ring of stages (mbarrier full / empty pairs, bounded waits);
-//  * warps 2-5 dequantise the packed INT4 codes (magic-number conversion,
+//  * warps 2.. (NG groups of four, taking the K steps in turn) dequantise
+//    the packed INT4 codes (magic-number conversion,
 //    group scale applied in fp16 as in the reference) and expand each 2:4
 //    pair to its four dense positions with byte permutes, writing the dense
 //    fp16 weight tile (128 x 64) into the stage in the UMMA K-major 128-byte
@@ -23,7 +24,7 @@
 //    K = 16 per instruction) with the weights as operand A and the
 //    activations as operand B, accumulating in fp32 in tensor memory, and
 //    frees each stage with tcgen05.commit;
-//  * warps 2-5 then read the accumulator (tcgen05.ld) and store C.
+//  * the same warps then read the accumulator (tcgen05.ld) and store C.
 //
 // The dense expansion doubles the tensor work against a sparse MMA (the
 // structured-sparse form needs the metadata in tensor memory in a layout
@@ -58,7 +59,11 @@ struct PrefillParams {
 
 constexpr int kPrefillSmemBudget = 227 * 1024;
 
-template <int BN>
+// NG groups of four dequantising warps take the K steps in turn (group
+// ks % NG).  The ring depth is a multiple of NG, so every slot belongs to one
+// group, which visits each of its uses in order (an mbarrier parity wait must
+// never skip a phase).
+template <int BN, int NG>
 struct PrefillCfg {
   static_assert(BN == 128 || BN == 256, "batch tile");
   static constexpr int ACT = BN * 128;                 // activation tile (BN rows x 64 K)
@@ -71,12 +76,13 @@ struct PrefillCfg {
   static constexpr int STAGE = (OFF_S + 256 + 1023) / 1024 * 1024;
   static constexpr int HEADER = 1024;
   static constexpr int DEPTH_FIT = (kPrefillSmemBudget - HEADER - 1024) / STAGE;
-  static constexpr int DEPTH = DEPTH_FIT > 8 ? 8 : DEPTH_FIT;
+  static constexpr int DEPTH_CAP = DEPTH_FIT > 8 ? 8 : DEPTH_FIT;
+  static constexpr int DEPTH = DEPTH_CAP / NG * NG;
   static constexpr int SMEM = HEADER + DEPTH * STAGE + 1024;
   static constexpr uint32_t TX_NOSCALE = ACT + 2048 + 1024;
   static constexpr uint32_t TX_SCALE = TX_NOSCALE + 256;
-  static constexpr int THREADS = 6 * 32;
-  static_assert(DEPTH >= 2, "prefill ring too shallow");
+  static constexpr int THREADS = (2 + 4 * NG) * 32;
+  static_assert(DEPTH >= 2 && DEPTH % NG == 0, "prefill ring too shallow");
 };
 
 // ---------------------------------------------------------------------------
@@ -175,10 +181,10 @@ __device__ __forceinline__ uint32_t expand_selector(uint32_t nib) {
   return (sel & 0xFFFFu) | ((sel >> 16) << 16);
 }
 
-template <int BN, bool GROUPED>
-__global__ void __launch_bounds__(PrefillCfg<BN>::THREADS, 1)
+template <int BN, int NG, bool GROUPED>
+__global__ void __launch_bounds__(PrefillCfg<BN, NG>::THREADS, 1)
     marlin24_prefill_kernel(const __grid_constant__ PrefillParams p) {
-  using Cfg = PrefillCfg<BN>;
+  using Cfg = PrefillCfg<BN, NG>;
   constexpr int D = Cfg::DEPTH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -273,9 +279,10 @@ __global__ void __launch_bounds__(PrefillCfg<BN>::THREADS, 1)
     }
   } else {
     // ---------------------------------------------- dequantise, then epilogue
-    const int dw = warp - 2;       // 0..3
+    const int dw = warp - 2;       // 0 .. 4*NG-1
+    const int grp = dw >> 2;       // this warp's group: K steps ks % NG == grp
     const int pr = dw & 1;         // 32-K row inside the 64-K step
-    const int cc = dw >> 1;        // 64-feature chunk inside the 128-feature tile
+    const int cc = (dw >> 1) & 1;  // 64-feature chunk inside the 128-feature tile
     const int g = lane >> 2;
     const int t = lane & 3;
     const uint32_t q_off = Cfg::OFF_B + pr * 1024 + cc * 512 + lane * 16;
@@ -289,7 +296,7 @@ __global__ void __launch_bounds__(PrefillCfg<BN>::THREADS, 1)
     const uint32_t half_off = 8 * (t & 1);
     const uint32_t sel_base = smem_addr(sel_tab);
     bool ok = true;
-    for (int ks = 0; ks < ksteps; ++ks) {
+    for (int ks = grp; ks < ksteps; ks += NG) {
       const int slot = ks % D;
       const uint32_t parity = (ks / D) & 1;
       if (!mbar_wait_bounded(smem_addr(&full_bar[slot]), parity, abort_flag)) {
@@ -358,7 +365,7 @@ __global__ void __launch_bounds__(PrefillCfg<BN>::THREADS, 1)
       if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n]);
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
 #pragma unroll 1
-      for (int cb = 0; cb < BN / 32; ++cb) {
+      for (int cb = grp; cb < BN / 32; cb += NG) {
         uint32_t v[32];
         tmem_ld32(lane_addr + cb * 32, v);
         const int b0 = m_tile * BN + cb * 32;

