@@ -8,7 +8,10 @@ Python surface mirrors the reference's ``marlin`` package
   (``__init__.py:45-58``, ``marlin_cuda.cpp:66-94``);
 * :mod:`csed499ii_b200.metadata_decode` -- the 3-bit metadata codec and the
   3-bit GEMM (``metadata_decode`` extension: ``pack``, ``unpack``, ``fetch``,
-  ``matmul``).
+  ``matmul``);
+* :class:`Layer_2_4` / :func:`replace_linear` -- the torch module surface
+  (``__init__.py:274-415``), packing on the GPU;
+* :mod:`csed499ii_b200.shard` -- column-parallel execution across GPUs.
 
 All compute runs in the in-tree CUDA library through its C ABI
 (``include/sm100_marlin.h``); nothing here computes on the CPU.
@@ -19,7 +22,7 @@ import torch
 
 from . import _ext
 
-__all__ = ["mul_2_4", "scratch_bytes", "device_status"]
+__all__ = ["mul_2_4", "scratch_bytes", "device_status", "Layer_2_4", "replace_linear"]
 
 
 def _stream_ptr(dev: int) -> int:
@@ -107,3 +110,6 @@ def scratch_bytes(prob_m: int, prob_n: int, prob_k: int, dev: int = 0, sms: int 
 def device_status(dev: int = 0) -> int:
     """Read and clear the device status word (nonzero = a bounded wait gave up)."""
     return _ext.device_status(dev)
+
+
+from .layer import Layer_2_4, replace_linear  # noqa: E402  (needs mul_2_4 above)

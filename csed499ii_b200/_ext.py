@@ -41,6 +41,8 @@ SIGNATURES = {
     "sm100_marlin_last_cuda_error": (ctypes.c_char_p, []),
     "sm100_marlin_set_trace_buffer": (_c_int, [_vp]),
     "sm100_marlin_set_overlap": (_c_int, [_c_int]),
+    "sm100_marlin_pack_2_4": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                                       _vp]),
 }
 
 OK = 0

@@ -21,6 +21,7 @@
 #include "device_primitives.cuh"
 #include "marlin24_gemm.cuh"
 #include "marlin24_prefill.cuh"
+#include "packer.cuh"
 #include "meta3_codec.cuh"
 
 namespace sm100 {
@@ -663,6 +664,39 @@ const char* sm100_marlin_error_string(int code) {
 }
 
 const char* sm100_marlin_last_cuda_error(void) { return t_last_cuda_error.c_str(); }
+
+int sm100_marlin_pack_2_4(const void* w, const void* s, int prob_k, int prob_m, int groupsize,
+                          void* B, void* meta, void* s_out, int dev, void* stream_v) {
+  if (prob_k <= 0 || prob_m <= 0 || prob_k % 128 != 0 || prob_m % 64 != 0)
+    return SM100_MARLIN_ERR_PROB_SHAPE;
+  if (groupsize != -1 && (groupsize <= 0 || prob_k % groupsize != 0))
+    return SM100_MARLIN_ERR_PROB_SHAPE;
+  if (!w || !s || !B || !meta || !s_out) return SM100_MARLIN_ERR_ARGUMENT;
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_v);
+  const int g_rows = groupsize == -1 ? prob_k : groupsize;
+  const int s_rows = prob_k / g_rows;
+  auto blocks = [](long long total) {
+    const long long b = (total + 255) / 256;
+    return static_cast<int>(b < 148 * 16 ? b : 148 * 16);
+  };
+  const long long b_words = static_cast<long long>(prob_k / 32) * 2 * prob_m;
+  const long long meta_words = static_cast<long long>(prob_m) * (prob_k / 16);
+  const long long s_words = static_cast<long long>(s_rows) * prob_m;
+  pack_b_kernel<<<blocks(b_words), 256, 0, stream>>>(static_cast<const half*>(w),
+                                                     static_cast<const half*>(s), prob_k, prob_m,
+                                                     g_rows, static_cast<uint32_t*>(B));
+  pack_meta_kernel<<<blocks(meta_words), 256, 0, stream>>>(static_cast<const half*>(w),
+                                                           static_cast<const half*>(s), prob_k,
+                                                           prob_m, g_rows,
+                                                           static_cast<uint16_t*>(meta));
+  pack_scales_kernel<<<blocks(s_words), 256, 0, stream>>>(static_cast<const half*>(s), s_rows, prob_m,
+                                                          groupsize != -1 ? 1 : 0,
+                                                          static_cast<half*>(s_out));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
 
 int sm100_marlin_set_overlap(int enable) {
   g_pdl_override = enable ? 1 : 0;

@@ -113,6 +113,20 @@ int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta,
                                  int thread_k, int thread_m, int sms, int max_par);
 
 /*
+ * GPU packer: fp16 weight w (prob_k, prob_m) row-major and unpermuted fp16
+ * scales s (prob_k/groupsize or 1, prob_m) -> B int32 (prob_k/32, 2*prob_m),
+ * meta int16 (prob_m, prob_k/16), s_out fp16 (same shape as s, permuted),
+ * bit-identical to `Layer_2_4.pack(linear, scales, trans=True)`
+ * (kernel_experiments/sparse_marlin/src/marlin/__init__.py:331-388: quantise
+ * clamp(round(w/s)+8, 0, 15), 2:4 mask on the biased codes, CUTLASS
+ * compression and metadata reorder, Marlin tiling and nibble packing), which
+ * the reference runs on the CPU.  groupsize is the uncompressed group (128)
+ * or -1; prob_k % 128 == 0 and prob_m % 64 == 0.  Asynchronous on `stream`.
+ */
+int sm100_marlin_pack_2_4(const void* w, const void* s, int prob_k, int prob_m, int groupsize,
+                          void* B, void* meta, void* s_out, int dev, void* stream);
+
+/*
  * 3-bit metadata codec.  Replaces `pack_metadata` / `unpack_metadata`
  * (kernel_experiments/sparse_marlin/metadata_decode/codec.cu:30-41).
  * pack:   meta int16[n_int16] (n_int16 % 128 == 0) -> out int32[n_int16*3/8];
