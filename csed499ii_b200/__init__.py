@@ -26,7 +26,7 @@ __all__ = ["mul_2_4", "scratch_bytes", "device_status", "Layer_2_4", "replace_li
 
 
 def _stream_ptr(dev: int) -> int:
-    return torch.cuda.current_stream(dev).cuda_stream
+    return torch._C._cuda_getCurrentRawStream(dev)
 
 
 def _check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype, dev: int) -> None:
@@ -62,28 +62,40 @@ def _raise_for(err: int, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize) 
     raise RuntimeError(f"sm100_marlin error {err}: {_ext.describe(err)}")
 
 
+_HALF, _INT32, _INT16 = torch.half, torch.int32, torch.int16
+
+
 def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bits):
-    lib = _ext.load()
-    prob_n = A.size(0)  # batch rows
-    prob_m = C.size(1)  # output features
-    prob_k = A.size(1)
+    lib = _ext._lib or _ext.load()
+    prob_n, prob_k = A.shape  # batch rows, input features
+    prob_m = C.shape[1]       # output features
     groupsize = _groupsize(prob_k, s)
     if workspace.numel() < prob_m // 128 * max_par:
         raise RuntimeError(f"workspace must be of size at least {prob_m // 128 * max_par}.")
     dev = A.get_device()
     if dev < 0:
         raise RuntimeError("A must be a CUDA tensor")
-    _check_cuda("A", A, torch.half, dev)
-    _check_cuda("B", B, torch.int32, dev)
-    _check_cuda("meta", meta, torch.int16 if meta_bits == 4 else torch.int32, dev)
-    _check_cuda("C", C, torch.half, dev)
-    _check_cuda("s", s, torch.half, dev)
-    _check_cuda("workspace", workspace, torch.int32, dev)
+    meta_dtype = _INT16 if meta_bits == 4 else _INT32
+    # one combined test on the hot path; the per-tensor checks (with their
+    # messages) only run when it fails
+    if not (A.dtype is _HALF and C.dtype is _HALF and s.dtype is _HALF and B.dtype is _INT32
+            and meta.dtype is meta_dtype and workspace.dtype is _INT32
+            and B.get_device() == dev and meta.get_device() == dev and C.get_device() == dev
+            and s.get_device() == dev and workspace.get_device() == dev
+            and A.is_contiguous() and B.is_contiguous() and meta.is_contiguous()
+            and C.is_contiguous() and s.is_contiguous() and workspace.is_contiguous()):
+        _check_cuda("A", A, _HALF, dev)
+        _check_cuda("B", B, _INT32, dev)
+        _check_cuda("meta", meta, meta_dtype, dev)
+        _check_cuda("C", C, _HALF, dev)
+        _check_cuda("s", s, _HALF, dev)
+        _check_cuda("workspace", workspace, _INT32, dev)
     fn = lib.sm100_marlin_mul_2_4 if meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
     err = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
              prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
              thread_m, sms, max_par)
-    _raise_for(err, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize)
+    if err:
+        _raise_for(err, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize)
 
 
 def mul_2_4(A, B, meta, C, s, workspace, thread_k=-1, thread_m=-1, sms=-1, max_par=16):

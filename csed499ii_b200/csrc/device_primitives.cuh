@@ -108,6 +108,12 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
+// Orders this thread's earlier (generic-proxy) accesses of global memory
+// before its later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Fire-and-forget add (no return value, so the issuing thread does not wait
 // for the round trip).  Callers order their earlier writes with a fence.
 __device__ __forceinline__ void red_add_relaxed_gpu(int* p, int v) {

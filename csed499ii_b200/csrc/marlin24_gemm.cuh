@@ -133,12 +133,19 @@ struct DecodeCfg {
   // slots per chunk let each level run in one pass, unless they would cost the
   // ring more than one stage.
   static constexpr int ring_depth(int slots) {
-    return (kSmemBudget - (HEADER + NC * slots * ACC_BYTES + 1023) / 1024 * 1024 - 1024) / STAGE;
+    return (kSmemBudget - (HEADER + NC * slots * ACC_BYTES + 1023) / 1024 * 1024 -
+            (MB == 1 ? 2 * NC * ACC_BYTES : 0) - 1024) / STAGE;
   }
   static constexpr int RED_SLOTS =
       (WPC / 2 > 1 && ring_depth(WPC / 2) + 1 >= ring_depth(1)) ? WPC / 2 : 1;
   static constexpr int RED_BYTES = NC * RED_SLOTS * ACC_BYTES;
-  static constexpr int RING_OFF = (HEADER + RED_BYTES + 1023) / 1024 * 1024;
+  // Split-K finisher: room for the partials of up to FIN_SLOTS other CTAs of
+  // its tile, bulk-copied in while the finisher still computes (batch <= 16;
+  // larger partials are read from global memory at the end).
+  static constexpr int FIN_SLOTS = MB == 1 ? 2 : 0;
+  static constexpr int FIN_BYTES = FIN_SLOTS * NC * ACC_BYTES;
+  static constexpr int FIN_OFF = (HEADER + RED_BYTES + 1023) / 1024 * 1024;
+  static constexpr int RING_OFF = (FIN_OFF + FIN_BYTES + 1023) / 1024 * 1024;
   static constexpr int DEPTH_FIT = (kSmemBudget - RING_OFF - 1024) / STAGE;
   static constexpr int DEPTH = DEPTH_FIT > 16 ? 16 : DEPTH_FIT;
   static constexpr int SMEM = RING_OFF + DEPTH * STAGE + 1024;   // +1024: base alignment slack
@@ -192,6 +199,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
   // of every other CTA of the finisher's tile are published.
   uint64_t* fin_bar = reinterpret_cast<uint64_t*>(smem + 520);
   uint8_t* red = smem + Cfg::HEADER;
+  uint8_t* fin = smem + Cfg::FIN_OFF;
   uint8_t* ring = smem + Cfg::RING_OFF;
 
   const int warp = threadIdx.x >> 5;
@@ -315,9 +323,25 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         if (u_begin <= t0 && u_end < t0 + units_per_tile) {
           const int others =
               static_cast<int>(unit_owner(t0 + units_per_tile - 1, p.units, grid) - cta);
-          if (!wait_counter_bounded(&p.counters[last_tile], others, abort_flag))
+          const uint32_t fb = smem_addr(fin_bar);
+          if (!wait_counter_bounded(&p.counters[last_tile], others, abort_flag)) {
             atomicOr(p.status, kStatusFinishWaitTimeout);
-          mbar_arrive(smem_addr(fin_bar));
+            mbar_arrive(fb);
+          } else {
+            // bring the first FIN_SLOTS partials next to the consumers
+            const int n_fin = others < Cfg::FIN_SLOTS ? others : Cfg::FIN_SLOTS;
+            constexpr uint32_t kPart = NC * Cfg::ACC_BYTES;
+            if (n_fin > 0) {
+              fence_proxy_async_global();
+              mbar_arrive_expect_tx(fb, n_fin * kPart);
+              for (int i = 0; i < n_fin; ++i)
+                bulk_g2s(smem_addr(fin) + i * kPart,
+                         p.partials + ((cta + 1 + i) * NC) * Cfg::ACC_F4 * 32, kPart, fb,
+                         policy_evict_first());
+            } else {
+              mbar_arrive(fb);
+            }
+          }
         }
       }
     }
@@ -565,9 +589,23 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       if (trace && threadIdx.x == 0) trace[6] += 1;
       const long long t0 = static_cast<long long>(tile) * units_per_tile;
       const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
-      // two contributors' loads in flight at a time, 8 float4 per lane each
+      // partials already in shared memory (bulk-copied by the producer)
+      const long long c_fin = cta + Cfg::FIN_SLOTS < c_hi ? cta + Cfg::FIN_SLOTS : c_hi;
+      for (long long c = cta + 1; c <= c_fin; ++c) {
+        const uint32_t src = smem_addr(fin) +
+                             ((static_cast<int>(c - cta - 1) * NC + cc) * Cfg::ACC_F4 * 32 + lane) * 16;
+#pragma unroll
+        for (int v = 0; v < Cfg::ACC_F4; ++v) {
+          const uint4 x = lds128(src + v * 512);
+          float4& a = acc4[v];
+          a.x += __uint_as_float(x.x); a.y += __uint_as_float(x.y);
+          a.z += __uint_as_float(x.z); a.w += __uint_as_float(x.w);
+        }
+      }
+      // the rest from global memory: two contributors' loads in flight at a
+      // time, 8 float4 per lane each
       constexpr int VB = Cfg::ACC_F4 < 8 ? Cfg::ACC_F4 : 8;
-      for (long long c = cta + 1; c <= c_hi; c += 2) {
+      for (long long c = c_fin + 1; c <= c_hi; c += 2) {
         const bool two = c + 1 <= c_hi;
         const float4* src0 = p.partials + ((c * NC + cc) * Cfg::ACC_F4) * 32 + lane;
         const float4* src1 = two ? src0 + NC * Cfg::ACC_F4 * 32 : src0;
