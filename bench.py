@@ -158,15 +158,32 @@ def bench_ours(args, torch, dist, rank, world, dev):
     devi = dev.index
     fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
     stream = torch.cuda.Stream(device=dev)
+    # N > 1, default: the all-gather fused into the GEMM epilogue (peer stores
+    # over NVLink into buffers shared by CUDA IPC); --gather nccl: separate
+    # NCCL all-gather after each GEMM
+    fused = world > 1 and args.gather == "fused"
+    fg = shard.FusedGather(M, max(N for _, N in SHAPES), device=dev) if fused else None
+    shards = [[shard.ShardedWeight.from_local(B, meta, s, rank * N, (rank + 1) * N, args.meta_bits)
+               for (K, N), (B, meta, s) in zip(SHAPES, lay)] for lay in layers] if fused else None
 
     def step_raw(s_ptr):
-        for lay in layers:
-            for (K, N), (B, meta, s) in zip(SHAPES, lay):
-                rc = fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(), s.data_ptr(),
-                        N, M, K, ws.data_ptr(), GROUP // 2, devi, s_ptr, -1, -1, -1, 16)
+        for li, lay in enumerate(layers):
+            for si, ((K, N), (B, meta, s)) in enumerate(zip(SHAPES, lay)):
+                if fused:
+                    b = fg.next
+                    fg.next ^= 1
+                    rc = lib.sm100_marlin_mul_2_4_gather(
+                        A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(), N, M, K,
+                        shards[li][si].workspace.data_ptr(), GROUP // 2, devi, s_ptr,
+                        args.meta_bits, fg._c[b], fg._flag[b], fg._seen[b], world, rank)
+                else:
+                    rc = fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(),
+                            s.data_ptr(), N, M, K, ws.data_ptr(), GROUP // 2, devi, s_ptr, -1, -1,
+                            -1, 16)
                 if rc != 0:
                     raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
-                gather(N)
+                if not fused:
+                    gather(N)
 
     bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
     launches_step = args.layers * len(SHAPES) * ((M + 63) // 64)
@@ -214,11 +231,19 @@ def bench_ours(args, torch, dist, rank, world, dev):
         g2 = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g2, stream=stream):
             sp = torch.cuda.current_stream(dev).cuda_stream
-            for lay in layers:
+            for li, lay in enumerate(layers):
                 B, meta, s = lay[idx]
-                fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(), s.data_ptr(),
-                   N, M, K, ws.data_ptr(), GROUP // 2, devi, sp, -1, -1, -1, 16)
-                gather(N)
+                if fused:
+                    b = fg.next
+                    fg.next ^= 1
+                    lib.sm100_marlin_mul_2_4_gather(
+                        A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(), N, M, K,
+                        shards[li][idx].workspace.data_ptr(), GROUP // 2, devi, sp,
+                        args.meta_bits, fg._c[b], fg._flag[b], fg._seen[b], world, rank)
+                else:
+                    fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(),
+                       s.data_ptr(), N, M, K, ws.data_ptr(), GROUP // 2, devi, sp, -1, -1, -1, 16)
+                    gather(N)
         for _ in range(3):
             g2.replay()
         torch.cuda.synchronize(dev)
@@ -238,15 +263,18 @@ def bench_ours(args, torch, dist, rank, world, dev):
     # ---- end to end through the public operator, host buffers
     A_h = {K: A[K].cpu().pin_memory() for K in A}
     C_h = {N: torch.empty((M, world * N), dtype=torch.half).pin_memory() for N in C}
-    C_out = Cg if world > 1 else C
+    C_out = dict(Cg) if world > 1 else C
     A_d = {K: torch.empty_like(A[K]) for K in A}
     e2e_steps = max(3, min(args.steps, 20))
 
     def e2e_step():
         for K in A_h:
             A_d[K].copy_(A_h[K], non_blocking=True)
-        for lay in layers:
-            for (K, N), (B, meta, s) in zip(SHAPES, lay):
+        for li, lay in enumerate(layers):
+            for si, ((K, N), (B, meta, s)) in enumerate(zip(SHAPES, lay)):
+                if fused:
+                    C_out[N] = shard.mul_2_4_gathered(A_d[K], shards[li][si], fg)
+                    continue
                 if args.meta_bits == 4:
                     m.mul_2_4(A_d[K], B, meta, C[N], s, ws)
                 else:
@@ -274,6 +302,14 @@ def bench_ours(args, torch, dist, rank, world, dev):
     e2e_value = bytes_step * world * e2e_steps / (e2e_ms * 1e-3) / 1e9
     h2d = sum(t.numel() * 2 for t in A_h.values())
     d2h = sum(t.numel() * 2 for t in C_h.values())
+
+    # the graphs hold launches that reference the fused-gather buffers
+    del graph
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    if fg is not None:
+        fg.close()
 
     peak, peak_kind = load_peaks()
     # DRAM bytes (read + write) per launch from one ncu capture of the same
@@ -391,6 +427,9 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--meta-bits", type=int, choices=[3, 4], default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: all-gather of C fused into the GEMM epilogue (NVLink peer "
+                         "stores) or a separate NCCL all-gather")
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
                     help="decode: Llama-2-7B decode step (config 1, the headline); "
                          "prefill: compute-bound sweep (config 4)")
@@ -409,8 +448,8 @@ def main():
                     f"({args.layers * 75.4 / 1024:.2f} GB) per step",
               "parallelism": ("single GPU" if args.gpus == 1 else
                               f"tp{args.gpus} column-parallel: each rank holds an N-wide shard of "
-                              f"{args.gpus}N-wide layers (weak scaling), NCCL all-gather of C after "
-                              f"every GEMM")}
+                              f"{args.gpus}N-wide layers (weak scaling), all-gather of C after "
+                              f"every GEMM ({'fused into the GEMM epilogue over NVLink' if args.gather == 'fused' else 'NCCL'})")}
     metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-7B decode layer set, M={args.m})"
 
     if args.impl == "reference":

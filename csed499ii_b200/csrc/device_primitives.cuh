@@ -21,6 +21,7 @@ enum : int {
   kStatusFullWaitTimeout = 1,    // consumer waited too long for a stage
   kStatusEmptyWaitTimeout = 2,   // producer waited too long for a free slot
   kStatusFinishWaitTimeout = 4,  // split-K finisher waited too long for partials
+  kStatusGatherWaitTimeout = 8,  // fused all-gather waited too long for other ranks' blocks
 };
 
 // Upper bound for any single wait, in nanoseconds of %globaltimer.
@@ -118,6 +119,22 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 // for the round trip).  Callers order their earlier writes with a fence.
 __device__ __forceinline__ void red_add_relaxed_gpu(int* p, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// System-scope counters for the fused all-gather between GPUs (peer memory
+// over NVLink).
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_add_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // Poll `*p` (acquire) until it reaches `target`.  Bounded like

@@ -45,6 +45,8 @@
 
 namespace sm100 {
 
+constexpr int kMaxGatherRanks = 8;
+
 struct GemmParams {
   CUtensorMap tm_a;     // A  fp16 (64, M rows, K/64) box (64, 16*MB, SK/2), 128B swizzle
   CUtensorMap tm_b;     // B  u64  (K/32 rows, N)     box (64*NC, SK)
@@ -65,6 +67,18 @@ struct GemmParams {
   unsigned long long* trace;  // optional per-CTA timestamps (SM100_MARLIN_TRACE builds)
   int pdl;              // launched with programmatic dependent launch
   int prefetch;         // stages whose weights may be issued before griddepcontrol.wait
+  // Fused all-gather of column-parallel shards (gather_world > 0): every C row
+  // this launch computes is stored into each rank's gathered buffer (peer
+  // memory over NVLink) at this rank's column block, then counted on each
+  // rank's arrival counter; CTA 0 returns only once its own counter shows the
+  // blocks of every rank for this call.
+  half* gather_c[kMaxGatherRanks];                   // each rank's gathered C (row 0 of this launch)
+  unsigned long long* gather_flag[kMaxGatherRanks];  // each rank's arrival counter
+  unsigned long long* gather_seen;                   // arrivals this rank has already waited for
+  long long gather_ldc;                              // row stride of the gathered C (elements)
+  int gather_world;                                  // 0: plain stores to C
+  int gather_rank;
+  int tiles_per_rank;                                // tiles each rank stores per call
 };
 
 // Per-CTA timeline written when the library is built with
@@ -357,6 +371,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
   uint32_t stage = 0;
   bool aborted = false;
   bool epi_waited = !p.pdl;
+  int tiles_stored = 0;  // tiles this CTA wrote to C (counted by thread 0)
 
   // Per-warp shared-memory offsets inside a stage, computed once: every
   // per-stage load is then (stage base + constant) with an immediate row
@@ -631,6 +646,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       if (cc == 0 && lane == 0) p.counters[tile] = 0;
     }
     // 3) the leader warp of each chunk converts and stores 16-byte rows of C.
+    if (threadIdx.x == 0) ++tiles_stored;
     {
       const int n0 = (tile * NC + cc) * 64 + 8 * g;
       float colscale[8];
@@ -665,8 +681,50 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
             half2* oh = reinterpret_cast<half2*>(&o);
 #pragma unroll
             for (int i = 0; i < 4; ++i) oh[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-            *reinterpret_cast<uint4*>(p.C + static_cast<long long>(r) * p.N + n0) = o;
+            if (p.gather_world == 0) {
+              *reinterpret_cast<uint4*>(p.C + static_cast<long long>(r) * p.N + n0) = o;
+            } else {
+              const long long off = static_cast<long long>(r) * p.gather_ldc +
+                                    static_cast<long long>(p.gather_rank) * p.N + n0;
+              for (int q = 0; q < p.gather_world; ++q)
+                *reinterpret_cast<uint4*>(p.gather_c[q] + off) = o;
+            }
           }
+    }
+  }
+  if (p.gather_world > 0) {
+    // every consumer warp's C stores precede thread 0's system-scope release
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (threadIdx.x == 0) {
+      if (tiles_stored > 0) {
+        fence_acq_rel_sys();
+        for (int q = 0; q < p.gather_world; ++q)
+          red_add_relaxed_sys_u64(p.gather_flag[q], static_cast<unsigned long long>(tiles_stored));
+      }
+      if (blockIdx.x == 0) {
+        // the launch completes only when this rank holds every rank's block:
+        // the arrival counter only grows; `seen` (device memory, so graph
+        // replays advance it too) is where the previous call's wait ended
+        const unsigned long long seen = *p.gather_seen;
+        const unsigned long long target =
+            seen + static_cast<unsigned long long>(p.gather_world) * p.tiles_per_rank;
+        const unsigned long long* own = p.gather_flag[p.gather_rank];
+        unsigned long long t0 = 0;
+        uint32_t polls = 0;
+        bool ok = true;
+        while (ld_acquire_sys_u64(own) < target) {
+          if ((++polls & 63u) != 0) continue;
+          const unsigned long long now = global_timer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kWaitLimitNs) {
+            atomicOr(p.status, kStatusGatherWaitTimeout);
+            ok = false;
+            break;
+          }
+        }
+        if (ok) *p.gather_seen = target;
+      }
     }
   }
   if (trace && threadIdx.x == 0) trace[4] = global_timer_ns();

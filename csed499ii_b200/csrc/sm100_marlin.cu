@@ -451,10 +451,18 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   return SM100_MARLIN_ERR_KERN_SHAPE;
 }
 
+// Fused all-gather targets of one call (see sm100_marlin_mul_2_4_gather).
+struct GatherArgs {
+  int world, rank;
+  void* const* c;
+  void* const* flag;
+  void* seen;
+};
+
 int mul_impl(const void* A, const void* B, const void* meta, void* C, const void* s, int prob_m,
              int prob_n, int prob_k, void* workspace, int groupsize, int dev, void* stream_v,
              int thread_k, int thread_m, int sms, int max_par, int meta_bits, void* scratch,
-             size_t scratch_bytes) {
+             size_t scratch_bytes, const GatherArgs* gather = nullptr) {
   (void)max_par;
   if (prob_m < 0 || prob_n < 0 || prob_k < 0) return SM100_MARLIN_ERR_ARGUMENT;
   int rc = check_reference_shape(prob_m, prob_n, prob_k, groupsize, &thread_k, &thread_m);
@@ -475,6 +483,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   }
   if (sms <= 0) return SM100_MARLIN_ERR_ARGUMENT;
 
+  if (gather && prob_n > 64) return SM100_MARLIN_ERR_ARGUMENT;
   if (meta_bits == 4 && prob_n > prefill_min_rows() && prob_m % 128 == 0 && prob_k % 64 == 0) {
     int* status = nullptr;
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
@@ -515,6 +524,27 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.trace = g_trace_buffer ? g_trace_buffer + g_trace_launch++ * kTraceLaunchWords : nullptr;
     p.pdl = pdl_enabled() ? 1 : 0;
     p.prefetch = prefetch_stages();
+    p.gather_world = 0;
+    p.gather_rank = 0;
+    p.gather_seen = nullptr;
+    p.gather_ldc = 0;
+    p.tiles_per_rank = 0;
+    for (int q = 0; q < kMaxGatherRanks; ++q) {
+      p.gather_c[q] = nullptr;
+      p.gather_flag[q] = nullptr;
+    }
+    if (gather) {
+      p.gather_world = gather->world;
+      p.gather_rank = gather->rank;
+      p.gather_seen = static_cast<unsigned long long*>(gather->seen);
+      p.gather_ldc = static_cast<long long>(gather->world) * prob_m;
+      p.tiles_per_rank = prob_m / (64 * pl.nc);
+      for (int q = 0; q < gather->world; ++q) {
+        p.gather_c[q] = static_cast<half*>(gather->c[q]);
+        p.gather_flag[q] = static_cast<unsigned long long*>(gather->flag[q]);
+      }
+      p.C = p.gather_c[gather->rank];
+    }
     rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
     if (rc != SM100_MARLIN_OK) return rc;
     rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream) : dispatch<false>(p, pl, dev, stream);
@@ -695,6 +725,69 @@ int sm100_marlin_pack_2_4(const void* w, const void* s, int prob_k, int prob_m, 
                                                           groupsize != -1 ? 1 : 0,
                                                           static_cast<half*>(s_out));
   const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+int sm100_marlin_mul_2_4_gather(const void* A, const void* B, const void* meta, const void* s,
+                                int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
+                                int dev, void* stream, int meta_bits, void* const* gathered_c,
+                                void* const* arrival, void* seen, int world, int rank) {
+  if (world < 1 || world > kMaxGatherRanks || rank < 0 || rank >= world) return SM100_MARLIN_ERR_ARGUMENT;
+  if (meta_bits != 3 && meta_bits != 4) return SM100_MARLIN_ERR_ARGUMENT;
+  if (!gathered_c || !arrival || !seen) return SM100_MARLIN_ERR_ARGUMENT;
+  for (int q = 0; q < world; ++q) {
+    if (!gathered_c[q] || !arrival[q] || (reinterpret_cast<uintptr_t>(gathered_c[q]) & 15u) ||
+        (reinterpret_cast<uintptr_t>(arrival[q]) & 7u))
+      return SM100_MARLIN_ERR_ALIGNMENT;
+  }
+  const GatherArgs g{world, rank, gathered_c, arrival, seen};
+  return mul_impl(A, B, meta, gathered_c[rank], s, prob_m, prob_n, prob_k, workspace, groupsize,
+                  dev, stream, -1, -1, -1, 16, meta_bits, nullptr, 0, &g);
+}
+
+int sm100_marlin_ipc_alloc(size_t bytes, int dev, void** ptr) {
+  if (!ptr || bytes == 0) return SM100_MARLIN_ERR_ARGUMENT;
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+int sm100_marlin_ipc_free(void* ptr, int dev) {
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+int sm100_marlin_ipc_get_handle(void* ptr, int dev, void* handle) {
+  if (!ptr || !handle) return SM100_MARLIN_ERR_ARGUMENT;
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e);
+  std::memcpy(handle, &h, sizeof(h));
+  return SM100_MARLIN_OK;
+}
+
+int sm100_marlin_ipc_open(const void* handle, int dev, void** ptr) {
+  if (!ptr || !handle) return SM100_MARLIN_ERR_ARGUMENT;
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+int sm100_marlin_ipc_close(void* ptr, int dev) {
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 

@@ -18,12 +18,14 @@ multiples of 64 columns (every BASELINE config-3 shard is a multiple of 256).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["column_range", "slice_packed", "gather_columns", "mul_2_4_sharded", "ShardedWeight"]
+__all__ = ["column_range", "slice_packed", "gather_columns", "mul_2_4_sharded", "ShardedWeight",
+           "FusedGather", "mul_2_4_gathered"]
 
 
 def column_range(n_out: int, rank: int, world: int) -> Tuple[int, int]:
@@ -81,6 +83,18 @@ def gather_columns(C_local: torch.Tensor, group=None, out: Optional[torch.Tensor
 class ShardedWeight:
     """This rank's slice of one packed 2:4 layer, ready for :func:`mul_2_4_sharded`."""
 
+    @classmethod
+    def from_local(cls, B, meta, s, c0: int, c1: int, meta_bits: int = 4):
+        """Wrap an already sliced shard (columns ``[c0, c1)`` of the layer)."""
+        self = cls.__new__(cls)
+        self.B, self.meta, self.s = B, meta, s
+        self.k_in = B.size(0) * 32
+        self.c0, self.c1 = c0, c1
+        self.n_out = None
+        self.meta_bits = meta_bits
+        self.workspace = torch.zeros((c1 - c0) // 128 * 16, dtype=torch.int32, device=B.device)
+        return self
+
     def __init__(self, B, meta, s, rank: int, world: int, meta_bits: int = 4):
         n_out = B.size(1) // 2
         self.n_out = n_out
@@ -103,3 +117,107 @@ def mul_2_4_sharded(A: torch.Tensor, shard: ShardedWeight, C: torch.Tensor, grou
     _mul(A, shard.B, shard.meta, C_local, shard.s, shard.workspace, -1, -1, -1, 16,
          shard.meta_bits)
     return gather_columns(C_local, group=group, out=C)
+
+
+class _DevArray:
+    """A raw device pointer seen as a torch tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr, shape, dtype):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape,
+                                         "typestr": dtype, "version": 3, "strides": None}
+
+
+class FusedGather:
+    """Output buffers for the GEMM with the all-gather fused into its epilogue.
+
+    Every rank of ``group`` allocates one device region (CUDA IPC) holding two
+    gathered outputs of up to ``max_rows x (world * max_cols)`` fp16 and, per
+    buffer, an arrival counter and a "seen" word; the regions are exported,
+    exchanged with ``all_gather_object`` and mapped into every rank.  Calls
+    alternate between the two buffers, so a rank that already stores the next
+    call's block never overwrites one another rank may still be reading (the
+    fused call completes only when its own buffer holds all blocks).  All
+    ranks must make the same sequence of calls.
+    """
+
+    def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
+        from . import _ext
+
+        self._lib = _ext.load()
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.max_rows, self.max_cols = max_rows, max_cols
+        self._c_bytes = (max_rows * self.world * max_cols * 2 + 255) // 256 * 256
+        total = 2 * self._c_bytes + 256
+        base = ctypes.c_void_p()
+        self._check(self._lib.sm100_marlin_ipc_alloc(total, self.dev, ctypes.byref(base)))
+        self._own = base.value
+        self._opened = []
+        bases = [self._own]
+        if self.world > 1:
+            handle = (ctypes.c_char * 64)()
+            self._check(self._lib.sm100_marlin_ipc_get_handle(self._own, self.dev, handle))
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            bases = []
+            for q, h in enumerate(handles):
+                if q == self.rank:
+                    bases.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                self._check(self._lib.sm100_marlin_ipc_open(h, self.dev, ctypes.byref(peer)))
+                self._opened.append(peer.value)
+                bases.append(peer.value)
+        self._c = [(ctypes.c_void_p * self.world)(*[b + i * self._c_bytes for b in bases])
+                   for i in range(2)]
+        self._flag = [(ctypes.c_void_p * self.world)(*[b + 2 * self._c_bytes + 8 * i for b in bases])
+                      for i in range(2)]
+        self._seen = [self._own + 2 * self._c_bytes + 128 + 8 * i for i in range(2)]
+        self.next = 0
+
+    def _check(self, err):
+        from . import _ext
+
+        if err != _ext.OK:
+            raise RuntimeError(f"fused all-gather setup failed: {_ext.describe(err)}")
+
+    def output(self, buf: int, rows: int, cols: int) -> torch.Tensor:
+        """This rank's gathered buffer ``buf`` as an ``(rows, world*cols)`` fp16 tensor."""
+        ptr = self._c[buf][self.rank]
+        return torch.as_tensor(_DevArray(ptr, (rows, self.world * cols), "<f2"), device=f"cuda:{self.dev}")
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (after a device sync)."""
+        torch.cuda.synchronize(self.dev)
+        for ptr in self._opened:
+            self._lib.sm100_marlin_ipc_close(ptr, self.dev)
+        self._opened = []
+        if self._own:
+            self._lib.sm100_marlin_ipc_free(self._own, self.dev)
+            self._own = 0
+
+
+def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather):
+    """``A @ W`` for the column-sharded W with the all-gather fused into the
+    GEMM: returns this rank's ``(M, world * N/world)`` fp16 result (a view of
+    the fused buffer, valid until the call after next)."""
+    from . import _ext, _groupsize, _stream_ptr
+
+    m, k = A.shape
+    cols = shard.c1 - shard.c0
+    if m > 64 or m > gather.max_rows or cols > gather.max_cols:
+        raise ValueError("fused all-gather: at most 64 (and max_rows) rows, max_cols columns")
+    if not (A.is_cuda and A.dtype == torch.half and A.is_contiguous()):
+        raise RuntimeError("A must be a contiguous CUDA half tensor")
+    buf = gather.next
+    gather.next ^= 1
+    dev = A.get_device()
+    err = gather._lib.sm100_marlin_mul_2_4_gather(
+        A.data_ptr(), shard.B.data_ptr(), shard.meta.data_ptr(), shard.s.data_ptr(), cols, m, k,
+        shard.workspace.data_ptr(), _groupsize(k, shard.s), dev, _stream_ptr(dev), shard.meta_bits,
+        gather._c[buf], gather._flag[buf], gather._seen[buf], gather.world, gather.rank)
+    if err != _ext.OK:
+        raise RuntimeError(f"fused sharded GEMM failed: {_ext.describe(err)}")
+    return gather.output(buf, m, cols)

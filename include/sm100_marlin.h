@@ -35,6 +35,7 @@ extern "C" {
 #define SM100_MARLIN_STATUS_FULL_WAIT_TIMEOUT 1
 #define SM100_MARLIN_STATUS_EMPTY_WAIT_TIMEOUT 2
 #define SM100_MARLIN_STATUS_FINISH_WAIT_TIMEOUT 4
+#define SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT 8
 
 /*
  * C[prob_n, prob_m] (fp16, row-major) = A[prob_n, prob_k] (fp16, row-major)
@@ -111,6 +112,39 @@ int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta,
                                  const void* s, int prob_m, int prob_n, int prob_k,
                                  void* workspace, int groupsize, int dev, void* stream,
                                  int thread_k, int thread_m, int sms, int max_par);
+
+/*
+ * Column-parallel GEMM with the all-gather of C fused into its epilogue.  No
+ * counterpart in the reference (which has no multi-GPU code); it replaces
+ * "local mul_2_4 + all-gather of C" across `world` ranks (one GPU each) that
+ * hold column shards of one layer (prob_m columns each, batch prob_n <= 64).
+ *   gathered_c[q]  rank q's gathered output, fp16 (prob_n, world*prob_m)
+ *                  row-major, mapped into this process (sm100_marlin_ipc_open)
+ *   arrival[q]     rank q's uint64 arrival counter for that buffer (zero at
+ *                  creation, never reset)
+ *   seen           this rank's uint64: arrivals already waited for on the
+ *                  buffer (zero at creation; advanced on the device)
+ * Every C row this rank computes is stored into all ranks' gathered buffers
+ * (peer stores over NVLink) at column block `rank`; the call completes on the
+ * stream once this rank's buffer holds every rank's block (bounded wait,
+ * SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT on expiry).  All ranks must issue
+ * the same sequence of calls on a buffer (shapes may differ between calls).  A rank may already store its next
+ * call's block while another still reads this one, so alternate two buffers
+ * between consecutive calls.
+ */
+int sm100_marlin_mul_2_4_gather(const void* A, const void* B, const void* meta, const void* s,
+                                int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
+                                int dev, void* stream, int meta_bits, void* const* gathered_c,
+                                void* const* arrival, void* seen, int world, int rank);
+
+/* Device buffers shared between processes (CUDA IPC) for the fused all-gather:
+ * allocate (zeroed), export a 64-byte handle, map a peer's buffer, unmap,
+ * free.  No counterpart in the reference. */
+int sm100_marlin_ipc_alloc(size_t bytes, int dev, void** ptr);
+int sm100_marlin_ipc_free(void* ptr, int dev);
+int sm100_marlin_ipc_get_handle(void* ptr, int dev, void* handle);
+int sm100_marlin_ipc_open(const void* handle, int dev, void** ptr);
+int sm100_marlin_ipc_close(void* ptr, int dev);
 
 /*
  * GPU packer: fp16 weight w (prob_k, prob_m) row-major and unpermuted fp16

@@ -87,3 +87,79 @@ def test_two_rank_nccl_all_gather():
     for _ in range(world):
         rank, rel_mae, rel_fro = q.get(timeout=5)
         assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (rank, rel_mae, rel_fro)
+
+
+def test_fused_gather_one_rank():
+    """The fused path with a single rank (its own buffer is the only peer):
+    alternating buffers, changing shapes, the device-side arrival accounting."""
+    import csed499ii_b200 as m
+
+    gather = shard.FusedGather(64, 4096, device=DEV)
+    try:
+        cases = [(4096, 4096, 16), (4096, 2048, 1), (1024, 4096, 64), (4096, 4096, 16),
+                 (2048, 1024, 5)]
+        for i, (N, K, M) in enumerate(cases):
+            W, B, s, meta = random_packed_problem(N, K, 128, seed=100 + i)
+            sw = shard.ShardedWeight(torch.from_numpy(B).to(DEV), torch.from_numpy(meta).to(DEV),
+                                     torch.from_numpy(s).to(DEV), 0, 1)
+            A = torch.from_numpy(activations(M, K, seed=i)).to(DEV)
+            C = shard.mul_2_4_gathered(A, sw, gather)
+            torch.cuda.synchronize()
+            assert C.shape == (M, N)
+            rel_mae, rel_fro, _ = errors(C, A.float() @ torch.from_numpy(W).to(DEV).float())
+            assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (i, rel_mae, rel_fro)
+        assert m.device_status(0) == 0
+    finally:
+        gather.close()
+
+
+def _fused_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import csed499ii_b200 as m
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    dev = torch.device("cuda", rank)
+    gather = shard.FusedGather(16, 12288 // world, device=dev)
+    try:
+        shapes = [(4096, 4096), (11008, 4096), (4096, 4096), (12288, 4096), (4096, 11008)]
+        for i, (N, K) in enumerate(shapes):
+            W, B, s, meta = random_packed_problem(N, K, 128, seed=200 + i)
+            sw = shard.ShardedWeight(torch.from_numpy(B).to(dev), torch.from_numpy(meta).to(dev),
+                                     torch.from_numpy(s).to(dev), rank, world)
+            A = torch.from_numpy(activations(16, K, seed=30 + i)).to(dev)
+            C = shard.mul_2_4_gathered(A, sw, gather)
+            torch.cuda.synchronize(dev)
+            rel_mae, rel_fro, _ = errors(C, A.float() @ torch.from_numpy(W).to(dev).float())
+            q.put((rank, i, rel_mae, rel_fro))
+        q.put((rank, -1, float(m.device_status(rank)), 0.0))
+        dist.barrier()
+    finally:
+        gather.close()
+        dist.destroy_process_group()
+
+
+def test_fused_gather_two_ranks():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs)
+    got = [q.get(timeout=5) for _ in range(world * 6)]
+    for rank, i, a, b in got:
+        if i < 0:
+            assert a == 0.0, f"rank {rank} device status {a}"
+        else:
+            assert a < REL_MAE_TOL and b <= REL_FRO_TOL, (rank, i, a, b)
