@@ -21,6 +21,7 @@
 #include "device_primitives.cuh"
 #include "marlin24_gemm.cuh"
 #include "marlin24_prefill.cuh"
+#include "marlin24_prefill_sparse.cuh"
 #include "packer.cuh"
 #include "meta3_codec.cuh"
 
@@ -388,6 +389,17 @@ int prefill_groups() {
   return v;
 }
 
+// Groups of dequantising warps for the sparse prefill kernel
+// (SM100_MARLIN_PREFILL_SPARSE_GROUPS=1|2|4, tuning knob; default 2).
+int prefill_groups_sparse() {
+  static const int v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_SPARSE_GROUPS");
+    const int g = e ? std::atoi(e) : 2;
+    return (g == 1 || g == 4) ? g : 2;
+  }();
+  return v;
+}
+
 template <int BN, int NG, bool GROUPED>
 int launch_prefill_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
   using Cfg = PrefillCfg<BN, NG>;
@@ -404,8 +416,85 @@ int launch_prefill_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
+// Structured-sparse prefill kernel (tcgen05.mma.sp) for K % 128 == 0
+// (SM100_MARLIN_PREFILL_SPARSE=0 selects the dense-expansion kernel; tuning
+// knob).  SM100_MARLIN_PREFILL_BN=128|256 forces its batch tile.
+bool prefill_sparse_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_SPARSE");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
+int prefill_forced_bn() {
+  static const int v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_BN");
+    const int b = e ? std::atoi(e) : 0;
+    return (b == 128 || b == 256) ? b : 0;
+  }();
+  return v;
+}
+
+template <int BN, int NG, bool GROUPED>
+int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
+  using Cfg = PrefillSpCfg<BN, NG>;
+  static bool attr_set[64] = {};
+  auto kern = marlin24_prefill_sp_kernel<BN, NG, GROUPED>;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const dim3 grid(p.N / 128, (p.M + BN - 1) / BN);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+// The structured-sparse form: K steps of 128, tensor maps with 4-row boxes.
+int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const void* meta,
+                       const void* s, int dev, int sms, cudaStream_t stream) {
+  const uint64_t N = p.N, K = p.K;
+  const int n_tiles = p.N / 128;
+  int bn = prefill_forced_bn();
+  if (bn == 0)
+    bn = (p.M >= 256 && static_cast<long long>(n_tiles) * ((p.M + 255) / 256) >= sms) ? 256 : 128;
+  int rc = encode_2d(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, static_cast<uint64_t>(p.M),
+                     2 * K, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 4,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 4,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (p.grouped) {
+    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, 1,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    std::memset(&p.tm_s, 0, sizeof(p.tm_s));
+  }
+  // dequantising groups: 2 by default (the sparse step needs no expansion);
+  // the 256-row tile's two-stage ring allows at most 2
+  int ng = prefill_groups_sparse();
+  if (bn == 256 && ng > 2) ng = 2;
+#define SM100_PREFILL_SP(BN_, NG_)                                                   \
+  if (bn == BN_ && ng == NG_)                                                        \
+    return p.grouped ? launch_prefill_sp_cfg<BN_, NG_, true>(p, dev, stream)        \
+                     : launch_prefill_sp_cfg<BN_, NG_, false>(p, dev, stream);
+  SM100_PREFILL_SP(128, 1)
+  SM100_PREFILL_SP(128, 2)
+  SM100_PREFILL_SP(128, 4)
+  SM100_PREFILL_SP(256, 1)
+  SM100_PREFILL_SP(256, 2)
+#undef SM100_PREFILL_SP
+  return SM100_MARLIN_ERR_KERN_SHAPE;
+}
+
 // C[M, N] = A . dequant(B, meta, s) for M > prefill_min_rows() (4-bit
-// metadata): one 128 x BN output tile per CTA on the tcgen05 kernel.
+// metadata): one 128 x BN output tile per CTA on the tcgen05 kernels.
 int mul_prefill(const void* A, const void* B, const void* meta, void* C, const void* s, int n_out,
                 int m_rows, int k_in, int groupsize, int dev, int sms, cudaStream_t stream,
                 int* status) {
@@ -417,6 +506,8 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   p.N = n_out;
   p.K = k_in;
   p.grouped = groupsize != -1 ? 1 : 0;
+  if (prefill_sparse_enabled() && k_in % 128 == 0)
+    return mul_prefill_sparse(p, A, B, meta, s, dev, sms, stream);
   const int n_tiles = n_out / 128;
   const int bn = (m_rows >= 256 && static_cast<long long>(n_tiles) * ((m_rows + 255) / 256) >= sms)
                      ? 256 : 128;
