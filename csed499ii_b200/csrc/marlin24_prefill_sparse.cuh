@@ -5,15 +5,15 @@
 // multiple of 128).
 //
 // Per CTA: one 128-feature x BN-row output tile over the whole K range, K in
-// steps of 128 (one 128-byte swizzle atom of compressed weights, two of
-// activations, four MMAs of K = 32).
+// steps of 64 (a 64-byte-swizzled tile of compressed weights, one 128-byte
+// swizzle atom of activations, two MMAs of K = 32), so 4-8 stages fit.
 //
-//  * warp 0 (one thread): TMA of the two activation atoms and of the packed
-//    codes (4 x 32-K rows), metadata and scale row of the 128 features;
+//  * warp 0 (one thread): TMA of the activation atom and of the packed codes
+//    (2 x 32-K rows), metadata and scale row of the 128 features;
 //  * warps 2.. (NG groups of four, K steps in turn): dequantise the INT4
 //    codes and apply the group scale (fp16, as the reference), storing the
 //    COMPRESSED values (two per group of four; no zero fill) into the UMMA
-//    K-major 128-byte-swizzled tile, and copy the metadata words of the step
+//    K-major 64-byte-swizzled tile, and copy the metadata words of the step
 //    into tensor memory (tcgen05.st; one 4-column-aligned slot per MMA);
 //  * warp 1 (one thread): tcgen05.mma.sp.cta_group::1.kind::f16 with the
 //    compressed weights as operand A, the activations as operand B and the
@@ -36,28 +36,40 @@ namespace sm100 {
 template <int BN, int NG>
 struct PrefillSpCfg {
   static_assert(BN == 128 || BN == 256, "batch tile");
-  static constexpr int ACT = 2 * BN * 128;             // two 64-K activation atoms
-  static constexpr int ATILE = 128 * 128;              // compressed weights: 128 rows x 64 halves
+  static constexpr int ACT = BN * 128;                 // one 64-K activation atom
+  static constexpr int ATILE = 128 * 64;               // compressed weights: 128 rows x 32 halves
   static constexpr int OFF_ACT = 0;
   static constexpr int OFF_A = ACT;
-  static constexpr int OFF_B = OFF_A + ATILE;          // 4 rows x 1024 B of packed codes
-  static constexpr int OFF_M = OFF_B + 4096;           // 4 rows x 512 B of metadata
-  static constexpr int OFF_S = OFF_M + 2048;           // one scale row (128 features)
+  static constexpr int OFF_B = OFF_A + ATILE;          // 2 rows x 1024 B of packed codes
+  static constexpr int OFF_M = OFF_B + 2048;           // 2 rows x 512 B of metadata
+  static constexpr int OFF_S = OFF_M + 1024;           // one scale row (128 features)
   static constexpr int STAGE = (OFF_S + 256 + 1023) / 1024 * 1024;
   static constexpr int HEADER = 1024;
   static constexpr int DEPTH_FIT = (kPrefillSmemBudget - HEADER - 1024) / STAGE;
   static constexpr int DEPTH_CAP = DEPTH_FIT > 8 ? 8 : DEPTH_FIT;
   static constexpr int DEPTH = DEPTH_CAP / NG * NG;
   static constexpr int SMEM = HEADER + DEPTH * STAGE + 1024;
-  static constexpr uint32_t TX_NOSCALE = ACT + 4096 + 2048;
+  static constexpr uint32_t TX_NOSCALE = ACT + 2048 + 1024;
   static constexpr uint32_t TX_SCALE = TX_NOSCALE + 256;
   static constexpr int THREADS = (2 + 4 * NG) * 32;
-  static constexpr int META_COLS = 16;  // per stage: 4 MMAs x 4-column-aligned metadata slots
+  static constexpr int META_COLS = 8;  // per stage: 2 MMAs x 4-column-aligned metadata slots
   static constexpr int TMEM_NEED = BN + DEPTH * META_COLS;
   static constexpr int TMEM_COLS = TMEM_NEED <= 128 ? 128 : (TMEM_NEED <= 256 ? 256 : 512);
   static_assert(DEPTH >= 2 && DEPTH % NG == 0, "sparse prefill ring too shallow");
   static_assert(TMEM_NEED <= 512, "tensor memory");
 };
+
+// Shared-memory descriptor of a K-major operand in the 64-byte swizzled
+// canonical layout (rows of 64 bytes, 8-row groups 512 bytes apart, swizzle
+// mode 4).
+__device__ __forceinline__ uint64_t umma_desc_sw64_k(uint32_t saddr) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
 
 __device__ __forceinline__ void umma_sp_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t e_tmem, uint32_t idesc, uint32_t accumulate) {
@@ -100,7 +112,7 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x;
   const int m_tile = blockIdx.y;
-  const int ksteps = p.K / 128;
+  const int ksteps = p.K / 64;
 
   if (threadIdx.x < D) {
     mbar_init(smem_addr(&full_bar[threadIdx.x]), 1);
@@ -142,12 +154,10 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
         const uint32_t full = smem_addr(&full_bar[slot]);
         const uint32_t st = ring_base + slot * Cfg::STAGE;
         mbar_arrive_expect_tx(full, tx);
-        tma_load_2d(st + Cfg::OFF_ACT, &p.tm_act, ks * 128, m_tile * BN, full, pol_keep);
-        tma_load_2d(st + Cfg::OFF_ACT + BN * 128, &p.tm_act, ks * 128 + 64, m_tile * BN, full,
-                    pol_keep);
-        tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 4, full, pol_stream);
-        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * 64, ks * 4, full, pol_stream);
-        if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks, full, pol_keep);
+        tma_load_2d(st + Cfg::OFF_ACT, &p.tm_act, ks * 64, m_tile * BN, full, pol_keep);
+        tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 2, full, pol_stream);
+        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * 64, ks * 2, full, pol_stream);
+        if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks >> 1, full, pol_keep);
       }
     }
   } else if (warp == 1) {
@@ -167,10 +177,9 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
         tc_fence_after();
         const uint32_t st = ring_base + slot * Cfg::STAGE;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = umma_desc_sw128_k(st + Cfg::OFF_A + kk * 32);
-          const uint64_t bd =
-              umma_desc_sw128_k(st + Cfg::OFF_ACT + (kk >> 1) * BN * 128 + (kk & 1) * 64);
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t ad = umma_desc_sw64_k(st + Cfg::OFF_A + kk * 32);
+          const uint64_t bd = umma_desc_sw128_k(st + Cfg::OFF_ACT + kk * 64);
           umma_sp_f16(tmem, ad, bd, tmem_e + slot * Cfg::META_COLS + 4 * kk, idesc,
                       (ks | kk) ? 1u : 0u);
         }
@@ -182,7 +191,8 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
     // ---------------------------------------------- dequantise, then epilogue
     const int dw = warp - 2;        // 0 .. 4*NG-1
     const int grp = dw >> 2;        // K steps ks % NG == grp
-    const int r = dw & 3;           // 32-K row of the step whose codes this warp converts
+    const int r = dw & 1;           // 32-K row of the step whose codes this warp converts
+    const int cc = (dw >> 1) & 1;   // and its 64-feature chunk
     const int quarter = warp & 3;   // tensor-memory lanes this warp may access
     const int g = lane >> 2, t = lane & 3;
     // metadata word of TMEM lane 32*quarter + lane: chunk quarter/2, word
@@ -200,13 +210,12 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
         break;
       }
       const uint32_t st = ring_base + slot * Cfg::STAGE;
-      // metadata of the four MMAs into this warp's lanes of the stage's slots
+      // metadata of the two MMAs into this warp's lanes of the stage's slots
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
+      for (int kk = 0; kk < 2; ++kk)
         tmem_st32(e_lane + slot * Cfg::META_COLS + 4 * kk, lds32(st + Cfg::OFF_M + kk * 512 + m_word));
-      // compressed weights of 32-K row r, both 64-feature chunks
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      // compressed weights of 32-K row r, chunk cc
+      {
         const uint4 q = lds128(st + Cfg::OFF_B + r * 1024 + cc * 512 + lane * 16);
         uint4 sv = make_uint4(0, 0, 0, 0);
         if (GROUPED) sv = lds128(st + Cfg::OFF_S + cc * 128 + g * 16);
@@ -227,10 +236,13 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
           }
           // rows: feature 64cc + 8g + j -> g + 16(4cc + j), feature + 4 -> + 8
           const int m_lo = g + 16 * (4 * cc + j);
-          const uint32_t row_lo = st + Cfg::OFF_A + m_lo * 128;
-          const uint32_t row_hi = row_lo + 8 * 128;
-          // compressed columns 16r + 2t (chunk 2r) and 16r + 8 + 2t (chunk 2r+1)
-          const uint32_t ca = ((2 * r) ^ g) << 4, cb = ((2 * r + 1) ^ g) << 4;
+          const uint32_t row_lo = st + Cfg::OFF_A + m_lo * 64;
+          const uint32_t row_hi = row_lo + 8 * 64;
+          // compressed columns 16r + 2t (16-byte chunk 2r) and 16r + 8 + 2t
+          // (chunk 2r+1) of a 64-byte row, swizzled with (row / 2) mod 4;
+          // rows m and m + 8 share the pattern
+          const uint32_t sx = (g >> 1) & 3;
+          const uint32_t ca = ((2 * r) ^ sx) << 4, cb = ((2 * r + 1) ^ sx) << 4;
           const uint32_t wo = 4 * t;
           sts32(row_lo + ca + wo, *reinterpret_cast<uint32_t*>(&lo0));
           sts32(row_lo + cb + wo, *reinterpret_cast<uint32_t*>(&hi0));

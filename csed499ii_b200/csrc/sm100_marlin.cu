@@ -390,12 +390,13 @@ int prefill_groups() {
 }
 
 // Groups of dequantising warps for the sparse prefill kernel
-// (SM100_MARLIN_PREFILL_SPARSE_GROUPS=1|2|4, tuning knob; default 2).
+// (SM100_MARLIN_PREFILL_SPARSE_GROUPS=1|2|4, tuning knob).  Default 4:
+// 1199 / 1246 / 1294 TFLOP/s for 1 / 2 / 4 groups over the prefill sweep.
 int prefill_groups_sparse() {
   static const int v = [] {
     const char* e = std::getenv("SM100_MARLIN_PREFILL_SPARSE_GROUPS");
-    const int g = e ? std::atoi(e) : 2;
-    return (g == 1 || g == 4) ? g : 2;
+    const int g = e ? std::atoi(e) : 4;
+    return (g == 1 || g == 2) ? g : 4;
   }();
   return v;
 }
@@ -452,21 +453,23 @@ int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) 
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
-// The structured-sparse form: K steps of 128, tensor maps with 4-row boxes.
+// The structured-sparse form: K steps of 64 (as the dense form).
 int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const void* meta,
                        const void* s, int dev, int sms, cudaStream_t stream) {
   const uint64_t N = p.N, K = p.K;
   const int n_tiles = p.N / 128;
+  // 256-row tiles unless they would leave more than a quarter of the SMs idle
+  // (measured: the 128-row tile is slower per CTA by ~2x on this kernel)
   int bn = prefill_forced_bn();
   if (bn == 0)
-    bn = (p.M >= 256 && static_cast<long long>(n_tiles) * ((p.M + 255) / 256) >= sms) ? 256 : 128;
+    bn = (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
   int rc = encode_2d(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, static_cast<uint64_t>(p.M),
                      2 * K, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 4,
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 2,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 4,
+  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 2,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   if (p.grouped) {
@@ -476,10 +479,7 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   } else {
     std::memset(&p.tm_s, 0, sizeof(p.tm_s));
   }
-  // dequantising groups: 2 by default (the sparse step needs no expansion);
-  // the 256-row tile's two-stage ring allows at most 2
-  int ng = prefill_groups_sparse();
-  if (bn == 256 && ng > 2) ng = 2;
+  const int ng = prefill_groups_sparse();
 #define SM100_PREFILL_SP(BN_, NG_)                                                   \
   if (bn == BN_ && ng == NG_)                                                        \
     return p.grouped ? launch_prefill_sp_cfg<BN_, NG_, true>(p, dev, stream)        \
@@ -489,6 +489,7 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   SM100_PREFILL_SP(128, 4)
   SM100_PREFILL_SP(256, 1)
   SM100_PREFILL_SP(256, 2)
+  SM100_PREFILL_SP(256, 4)
 #undef SM100_PREFILL_SP
   return SM100_MARLIN_ERR_KERN_SHAPE;
 }
