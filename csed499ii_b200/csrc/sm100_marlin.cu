@@ -453,6 +453,43 @@ int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) 
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
+// CTA-pair form: 2-CTA clusters along the features, grid (N/128, M/256).
+template <int NG, bool GROUPED>
+int launch_prefill_sp2_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
+  using Cfg = PrefillSp2Cfg<NG>;
+  static bool attr_set[64] = {};
+  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED>;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.N / 128, (p.M + 255) / 256);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+// SM100_MARLIN_PREFILL_PAIR=0 keeps 256-row prefill tiles on one CTA
+// (tuning / comparison knob; default: CTA pairs).
+bool prefill_pair_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
+
 // The structured-sparse form: K steps of 64 (as the dense form).
 int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const void* meta,
                        const void* s, int dev, int sms, cudaStream_t stream) {
@@ -463,13 +500,29 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   int bn = prefill_forced_bn();
   if (bn == 0)
     bn = (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
-  int rc = encode_2d(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, static_cast<uint64_t>(p.M),
-                     2 * K, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  // a 256-row tile on a CTA pair (each CTA holds 128 of the rows) when the
+  // pair's 256 features divide N
+  const bool pair = bn == 256 && p.N % 256 == 0 && prefill_pair_enabled();
+  int rc;
+  if (pair) {
+    // (64 halves, M rows, K/64 slices), box 64 x 128 rows x 2 slices: the two
+    // 128-byte-swizzled 64-K atoms of one 128-K step for one CTA's 128 rows
+    const uint64_t a_dims[3] = {64, static_cast<uint64_t>(p.M), K / 64};
+    const uint64_t a_strides[2] = {2 * K, 128};
+    const uint32_t a_box[3] = {64, 128, 2};
+    rc = encode_nd(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, 3, a_dims, a_strides, a_box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    rc = encode_2d(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, K, static_cast<uint64_t>(p.M),
+                   2 * K, 64, bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   if (rc) return rc;
-  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 2,
+  // packed codes / metadata: 2 rows of 32 K per 64-K step, 4 per 128-K step (pair)
+  const uint32_t rows32 = pair ? 4 : 2;
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, rows32,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 2,
+  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, rows32,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   if (p.grouped) {
@@ -479,6 +532,9 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   } else {
     std::memset(&p.tm_s, 0, sizeof(p.tm_s));
   }
+  if (pair)
+    return p.grouped ? launch_prefill_sp2_cfg<4, true>(p, dev, stream)
+                     : launch_prefill_sp2_cfg<4, false>(p, dev, stream);
   const int ng = prefill_groups_sparse();
 #define SM100_PREFILL_SP(BN_, NG_)                                                   \
   if (bn == BN_ && ng == NG_)                                                        \

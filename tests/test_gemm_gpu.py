@@ -190,6 +190,29 @@ def test_prefill_per_column_scales(K):
     check(run(A, B, meta, s, 512, 64, 256), oracle_c(A, W))
 
 
+# 256-row tiles on CTA pairs (tcgen05.mma.sp.cta_group::2, N % 256 == 0): a
+# small `sms` makes the launcher choose the 256-row tile; ragged batches put
+# the odd CTA's rows partly or wholly past M; both scale modes.
+@pytest.mark.parametrize("K,N,M,g", [(512, 1024, 300, 128), (1024, 2048, 129, 128),
+                                     (1024, 1536, 257, -1), (2048, 512, 640, 128),
+                                     (4096, 4096, 1000, 128)])
+def test_prefill_pair(K, N, M, g):
+    if g == -1:
+        W, B, s, meta = quantized_problem(N, K, -1, seed=K + N)
+    else:
+        W, B, s, meta = random_packed_problem(N, K, 128, seed=K + N + M)
+    A = activations(M, K, seed=M + 1)
+    check(run(A, B, meta, s, N, sms=8), oracle_c(A, W))
+
+
+def test_prefill_pair_deterministic():
+    W, B, s, meta = random_packed_problem(2048, 1024, 128, seed=14)
+    A = activations(384, 1024, seed=15)
+    C0 = run(A, B, meta, s, 2048, sms=8)
+    for _ in range(3):
+        assert torch.equal(run(A, B, meta, s, 2048, sms=8), C0)
+
+
 def test_prefill_deterministic():
     W, B, s, meta = random_packed_problem(1024, 2048, 128, seed=12)
     A = activations(384, 2048, seed=13)
