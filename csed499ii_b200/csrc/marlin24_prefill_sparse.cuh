@@ -4,20 +4,24 @@
 // marlin24_prefill_kernel (the dense-expansion form, kept for K not a
 // multiple of 128).
 //
-// Per CTA: one 128-feature x BN-row output tile over the whole K range, K in
-// steps of 64 (a 64-byte-swizzled tile of compressed weights, one 128-byte
-// swizzle atom of activations, two MMAs of K = 32), so 4-8 stages fit.
+// Two forms.  The CTA-pair form further below (tcgen05.mma.sp.cta_group::2,
+// 128-K steps) runs every prefill whose N is a multiple of 256.  The
+// one-CTA form here (128-feature x BN-row tile, 64-K steps: a 64-byte-
+// swizzled tile of compressed weights, one 128-byte swizzle atom of
+// activations, two MMAs of K = 32, 4-8 stages) runs when pairs are off.
 //
-//  * warp 0 (one thread): TMA of the activation atom and of the packed codes
-//    (2 x 32-K rows), metadata and scale row of the 128 features;
+//  * warp 0 (lane 0 issues): TMA of the activation atom (counted on the
+//    ready barrier) and of the packed codes (2 x 32-K rows), metadata and
+//    scale row of the 128 features (counted on the weight barrier);
 //  * warps 2.. (NG groups of four, K steps in turn): dequantise the INT4
 //    codes and apply the group scale (fp16, as the reference), storing the
 //    COMPRESSED values (two per group of four; no zero fill) into the UMMA
 //    K-major 64-byte-swizzled tile, and copy the metadata words of the step
 //    into tensor memory (tcgen05.st; one 4-column-aligned slot per MMA);
-//  * warp 1 (one thread): tcgen05.mma.sp.cta_group::1.kind::f16 with the
-//    compressed weights as operand A, the activations as operand B and the
-//    metadata slot of each MMA; tcgen05.commit frees the stage.
+//  * warp 1 (lane 0 issues): one wait per K step on the ready barrier, then
+//    tcgen05.mma.sp.cta_group::1.kind::f16 with the compressed weights as
+//    operand A, the activations as operand B and the metadata slot of each
+//    MMA; tcgen05.commit frees the stage.
 //
 // Metadata layout in tensor memory (M = 128, K = 32 per MMA): lane
 // L = (m mod 8) + 8h + 16(m div 16) holds, in bits 0-15, the four nibbles of
@@ -119,8 +123,8 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
   const int ksteps = p.K / 64;
 
   if (threadIdx.x < D) {
-    mbar_init(smem_addr(&full_bar[threadIdx.x]), 1);
-    mbar_init(smem_addr(&aready_bar[threadIdx.x]), 4);
+    mbar_init(smem_addr(&full_bar[threadIdx.x]), 1);    // packed codes, metadata, scales
+    mbar_init(smem_addr(&aready_bar[threadIdx.x]), 5);  // activations (tx) + 4 dequant warps
     mbar_init(smem_addr(&empty_bar[threadIdx.x]), 1);
   }
   if (threadIdx.x == 32) {
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
     // the rest of its warp waits at the CTA barrier below runs slowly.
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
-    const uint32_t tx = Cfg::ACT + 2048 + 1024 + (GROUPED ? 256 : 0);
+    const uint32_t txw = 2048 + 1024 + (GROUPED ? 256 : 0);
     for (int ks = 0; ks < ksteps; ++ks) {
       const int slot = ks % D;
       const uint32_t parity = ((ks / D) & 1) ^ 1;
@@ -159,9 +163,11 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
       }
       if (lane == 0) {
         const uint32_t full = smem_addr(&full_bar[slot]);
+        const uint32_t ready = smem_addr(&aready_bar[slot]);
         const uint32_t st = ring_base + slot * Cfg::STAGE;
-        mbar_arrive_expect_tx(full, tx);
-        tma_load_2d(st + Cfg::OFF_ACT, &p.tm_act, ks * 64, m_tile * BN, full, pol_keep);
+        mbar_arrive_expect_tx(full, txw);
+        mbar_arrive_expect_tx(ready, Cfg::ACT);
+        tma_load_2d(st + Cfg::OFF_ACT, &p.tm_act, ks * 64, m_tile * BN, ready, pol_keep);
         tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 2, full, pol_stream);
         tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * 64, ks * 2, full, pol_stream);
         if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks >> 1, full, pol_keep);
@@ -181,13 +187,13 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
       constexpr uint64_t kStageDesc = Cfg::STAGE >> 4;  // start-address field step
       const uint64_t ad0 = umma_desc_sw64_k(ring_base + Cfg::OFF_A);
       const uint64_t bd0 = umma_desc_sw128_k(ring_base + Cfg::OFF_ACT);
-      const uint32_t full0 = smem_addr(full_bar), ready0 = smem_addr(aready_bar);
+      const uint32_t ready0 = smem_addr(aready_bar);
       const uint32_t empty0 = smem_addr(empty_bar);
       uint64_t ad = ad0, bd = bd0;
       uint32_t e = tmem_e, slot = 0, parity = 0;
       for (int ks = 0; ks < ksteps; ++ks) {
-        const bool ok = mbar_wait_bounded(full0 + 8 * slot, parity, abort_flag) &&
-                        mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
+        // one wait per step: activations landed and the tile dequantised
+        const bool ok = mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
           break;
@@ -344,8 +350,9 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
 //
 // Barriers per ring slot:
 //   wfull  (each CTA)  packed codes, metadata, scales landed     (count 1 + tx)
-//   afull  (even CTA)  both CTAs' activation halves landed        (count 1 + tx)
-//   aready (even CTA)  both CTAs' dequantised tiles + metadata    (count 8)
+//   aready (even CTA)  both CTAs' activation halves landed and both CTAs'
+//                      tiles dequantised (count 9 + tx): the MMA thread's
+//                      only wait per step (each wait costs it ~250 cycles)
 //   empty  (each CTA)  MMAs of the slot done (commit, multicast to the pair)
 // ===========================================================================
 
@@ -375,7 +382,7 @@ struct PrefillSp2Cfg {
   static constexpr int TMEM_COLS = TMEM_NEED <= 256 ? 256 : 512;
   static_assert(DEPTH >= 2 && DEPTH % NG == 0, "paired sparse prefill ring too shallow");
   static_assert(TMEM_NEED <= 512, "tensor memory");
-  static_assert((4 * DEPTH + 1) * 8 <= HEADER - 8, "barriers exceed the header");
+  static_assert((3 * DEPTH + 1) * 8 <= HEADER - 8, "barriers exceed the header");
 };
 
 __device__ __forceinline__ uint32_t cluster_cta_rank() {
@@ -474,8 +481,7 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* wfull_bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* afull_bar = wfull_bar + D;
-  uint64_t* aready_bar = afull_bar + D;
+  uint64_t* aready_bar = wfull_bar + D;
   uint64_t* empty_bar = aready_bar + D;
   uint64_t* acc_bar = empty_bar + D;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 1024 - 8);
@@ -491,8 +497,8 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
 
   if (threadIdx.x < D) {
     mbar_init(smem_addr(&wfull_bar[threadIdx.x]), 1);
-    mbar_init(smem_addr(&afull_bar[threadIdx.x]), 1);
-    mbar_init(smem_addr(&aready_bar[threadIdx.x]), 8);
+    // the pair's 8 dequantising-group warps + the even CTA's activation expect_tx
+    mbar_init(smem_addr(&aready_bar[threadIdx.x]), 9);
     mbar_init(smem_addr(&empty_bar[threadIdx.x]), 1);
   }
   if (threadIdx.x == 32) {
@@ -546,11 +552,11 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
         tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 4, wfull, pol_stream);
         tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * 64, ks * 4, wfull, pol_stream);
         if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks, wfull, pol_keep);
-        // both CTAs' activation halves count on the even CTA's barrier
-        const uint32_t afull = smem_addr(&afull_bar[slot]);
-        if (rank == 0) mbar_arrive_expect_tx(afull, Cfg::TX_ACT_PAIR);
+        // both CTAs' activation halves count on the even CTA's ready barrier
+        const uint32_t ready = smem_addr(&aready_bar[slot]);
+        if (rank == 0) mbar_arrive_expect_tx(ready, Cfg::TX_ACT_PAIR);
         // (64 halves, rows, K/64 slices): both 64-K atoms of the step in one copy
-        tma_load_3d_pair(st + Cfg::OFF_ACT, &p.tm_act, 0, act_row, ks * 2, mapa_shared(afull, 0),
+        tma_load_3d_pair(st + Cfg::OFF_ACT, &p.tm_act, 0, act_row, ks * 2, mapa_shared(ready, 0),
                          pol_keep);
       }
       __syncwarp();
@@ -564,13 +570,13 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
       constexpr uint64_t kAtomDesc = Cfg::ATOM >> 4;
       const uint64_t ad0 = umma_desc_sw128_k(ring_base + Cfg::OFF_A);
       const uint64_t bd0 = umma_desc_sw128_k(ring_base + Cfg::OFF_ACT);
-      const uint32_t full0 = smem_addr(afull_bar), ready0 = smem_addr(aready_bar);
+      const uint32_t ready0 = smem_addr(aready_bar);
       const uint32_t empty0 = smem_addr(empty_bar);
       uint64_t ad = ad0, bd = bd0;
       uint32_t e = tmem_e, slot = 0, parity = 0;
       for (int ks = 0; ks < ksteps; ++ks) {
-        const bool ok = mbar_wait_bounded(full0 + 8 * slot, parity, abort_flag) &&
-                        mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
+        // one wait per step: activations landed and both CTAs' tiles dequantised
+        const bool ok = mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
           break;

@@ -495,14 +495,15 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
                        const void* s, int dev, int sms, cudaStream_t stream) {
   const uint64_t N = p.N, K = p.K;
   const int n_tiles = p.N / 128;
-  // 256-row tiles unless they would leave more than a quarter of the SMs idle
-  // (measured: the 128-row tile is slower per CTA by ~2x on this kernel)
+  // CTA pairs (256 features x 256 rows, 128-K steps) whenever the pair's 256
+  // features divide N: per SM they do twice the work per K step of a one-CTA
+  // tile, so they win even where half of the pair's rows lie past M.  Else
+  // one CTA per tile: 256-row tiles unless they would leave more than a
+  // quarter of the SMs idle (the 128-row tile is ~2x slower per CTA).
   int bn = prefill_forced_bn();
+  const bool pair = p.N % 256 == 0 && prefill_pair_enabled() && bn != 128;
   if (bn == 0)
-    bn = (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
-  // a 256-row tile on a CTA pair (each CTA holds 128 of the rows) when the
-  // pair's 256 features divide N
-  const bool pair = bn == 256 && p.N % 256 == 0 && prefill_pair_enabled();
+    bn = pair || (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
   int rc;
   if (pair) {
     // (64 halves, M rows, K/64 slices), box 64 x 128 rows x 2 slices: the two

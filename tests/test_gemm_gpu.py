@@ -205,6 +205,57 @@ def test_prefill_pair(K, N, M, g):
     check(run(A, B, meta, s, N, sms=8), oracle_c(A, W))
 
 
+_SINGLE_CTA_SCRIPT = r"""
+import json, sys
+import numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from problems import activations, errors, quantized_problem, random_packed_problem
+import csed499ii_b200 as m
+torch.backends.cuda.matmul.allow_tf32 = False
+out = []
+for K, N, M, g, sms in [(1024, 512, 300, 128, -1), (512, 768, 200, -1, -1),
+                        (2048, 1024, 1000, 128, 8), (1024, 1536, 257, -1, 8)]:
+    if g == -1:
+        W, B, s, meta = quantized_problem(N, K, -1, seed=K + N)
+    else:
+        W, B, s, meta = random_packed_problem(N, K, 128, seed=K + N + M)
+    A = activations(M, K, seed=M + 2)
+    dev = "cuda:0"
+    C = torch.zeros((M, N), dtype=torch.half, device=dev)
+    ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
+    m.mul_2_4(torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev), torch.from_numpy(meta).to(dev),
+              C, torch.from_numpy(s).to(dev), ws, -1, -1, sms, 16)
+    torch.cuda.synchronize()
+    ref = torch.from_numpy(A).to(dev).float() @ torch.from_numpy(W).to(dev).float()
+    rel_mae, rel_fro, _ = errors(C, ref)
+    out.append([K, N, M, g, sms, rel_mae, rel_fro, bool(torch.isfinite(C).all())])
+out.append(m.device_status(0))
+print(json.dumps(out))
+"""
+
+
+# One CTA per 128-feature tile (tcgen05.mma.sp.cta_group::1), the form used
+# when CTA pairs are switched off (SM100_MARLIN_PREFILL_PAIR=0, read once per
+# process, hence the child process): 128- and 256-row batch tiles (a small
+# `sms` selects 256), ragged batches, both scale modes.
+def test_prefill_single_cta():
+    import json
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, SM100_MARLIN_PREFILL_PAIR="0",
+               PYTHONPATH=os.pathsep.join([os.path.dirname(here), os.path.join(os.path.dirname(here), "oracle"),
+                                           os.environ.get("PYTHONPATH", "")]))
+    res = subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT, here], env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    assert out[-1] == 0, f"device status {out[-1]}"
+    for K, N, M, g, sms, rel_mae, rel_fro, finite in out[:-1]:
+        assert finite and rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (K, N, M, g, sms, rel_mae, rel_fro)
+
+
 def test_prefill_pair_deterministic():
     W, B, s, meta = random_packed_problem(2048, 1024, 128, seed=14)
     A = activations(384, 1024, seed=15)
