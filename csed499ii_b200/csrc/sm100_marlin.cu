@@ -533,10 +533,18 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   } else {
     std::memset(&p.tm_s, 0, sizeof(p.tm_s));
   }
-  if (pair)
-    return p.grouped ? launch_prefill_sp2_cfg<4, true>(p, dev, stream)
-                     : launch_prefill_sp2_cfg<4, false>(p, dev, stream);
   const int ng = prefill_groups_sparse();
+  if (pair) {
+#define SM100_PREFILL_SP2(NG_)                                                       \
+  if (ng == NG_)                                                                     \
+    return p.grouped ? launch_prefill_sp2_cfg<NG_, true>(p, dev, stream)            \
+                     : launch_prefill_sp2_cfg<NG_, false>(p, dev, stream);
+    SM100_PREFILL_SP2(1)
+    SM100_PREFILL_SP2(2)
+    SM100_PREFILL_SP2(4)
+#undef SM100_PREFILL_SP2
+    return SM100_MARLIN_ERR_KERN_SHAPE;
+  }
 #define SM100_PREFILL_SP(BN_, NG_)                                                   \
   if (bn == BN_ && ng == NG_)                                                        \
     return p.grouped ? launch_prefill_sp_cfg<BN_, NG_, true>(p, dev, stream)        \
