@@ -48,6 +48,7 @@ struct PrefillParams {
   CUtensorMap tm_b;     // B as u64, dims (N, K/32), box (128, 2)
   CUtensorMap tm_meta;  // meta as u64, dims (N/2, K/32), box (64, 2)
   CUtensorMap tm_s;     // s as u64, dims (N/4, K/128), box (32, 1)   (grouped only)
+  CUtensorMap tm_c;     // C fp16, dims (N, M), box (128, 256)        (CTA-pair form only)
   const uint8_t* s;     // fp16 scales (per-column scaling in the epilogue)
   half* C;              // fp16 (M, N) row-major
   int* status;          // device status word

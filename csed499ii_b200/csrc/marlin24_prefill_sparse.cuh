@@ -440,6 +440,21 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap,
       : "memory");
 }
 
+__device__ __forceinline__ void sts16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
+// 2-D tiled TMA store shared -> global (rows past the tensor's end are
+// clipped by the copy), then wait until it has completed.
+__device__ __forceinline__ void tma_store_2d_wait(const void* tmap, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t slot_smem, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
                "r"(cols)
@@ -679,30 +694,38 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    // The ring is idle once the last MMA has completed: the CTA's 256 x 128
+    // fp16 block of C is assembled there (row b at 256 B, feature f at 2f;
+    // the 32 lanes of a store hit 16 distinct banks) and written by one TMA
+    // tensor store, which also clips rows past M.
+    bool stored = false;
     if (ok && mbar_wait_bounded(smem_addr(acc_bar), 0, abort_flag)) {
       tc_fence_after();
       const int rr = 32 * quarter + lane;
       const int m2 = rr >> 4;
       const int feat = 64 * (m2 >> 2) + 8 * (rr & 7) + (m2 & 3) + 4 * ((rr >> 3) & 1);
-      const int n = n_tile * 128 + feat;
       float cs = 1.f;
-      if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n]);
+      if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n_tile * 128 + feat]);
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+      const uint32_t c_col = ring_base + 2 * feat;
 #pragma unroll 1
       for (int cb2 = grp; cb2 < Cfg::BN / 32; cb2 += NG) {
         uint32_t v[32];
         tmem_ld32(lane_addr + cb2 * 32, v);
-        const int b0 = m_tile * 256 + cb2 * 32;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int b = b0 + j;
-          if (b < p.M)
-            p.C[static_cast<long long>(b) * p.N + n] = __float2half_rn(__uint_as_float(v[j]) * cs);
-        }
+        for (int j = 0; j < 32; ++j)
+          sts16(c_col + (cb2 * 32 + j) * 256,
+                __half_as_ushort(__float2half_rn(__uint_as_float(v[j]) * cs)));
       }
+      fence_proxy_async_smem();
+      stored = true;
     } else if (ok && lane == 0) {
       atomicOr(p.status, kStatusFullWaitTimeout);
     }
+    // all dequantising warps' parts of the block are in shared memory
+    named_bar_sync(1, 4 * NG * 32);
+    if (stored && warp == 2 && lane == 0 && *abort_flag == 0)
+      tma_store_2d_wait(&p.tm_c, ring_base, n_tile * 128, m_tile * 256);
   }
 
   // Teardown: every MMA of the pair must be complete (acc_bar, bounded) before

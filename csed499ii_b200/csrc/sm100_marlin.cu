@@ -535,6 +535,10 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   }
   const int ng = prefill_groups_sparse();
   if (pair) {
+    // C as (N, M) fp16, box 128 features x 256 rows: one TMA store per CTA
+    rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.C, N, static_cast<uint64_t>(p.M),
+                   2 * N, 128, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
 #define SM100_PREFILL_SP2(NG_)                                                       \
   if (ng == NG_)                                                                     \
     return p.grouped ? launch_prefill_sp2_cfg<NG_, true>(p, dev, stream)            \
