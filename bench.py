@@ -418,6 +418,44 @@ def bench_prefill(args, torch, dev):
     return flops_total / sec_total / 1e12, detail
 
 
+def bench_cusparselt(args, torch, dev):
+    """Library bar for the prefill sweep, as the reference's own comparator
+    (kernel_bench/bench.py:249-277): an fp16 2:4 GEMM through cuSPARSELt
+    (torch._cslt_compress / torch._cslt_sparse_mm) on the same shapes, fp16
+    weights (4x the bytes of the INT4 ones), timed the same way."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4322)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.Stream(device=dev)
+    detail, flops_total, sec_total = {}, 0.0, 0.0
+    for (K, N) in PREFILL_SHAPES:
+        W = torch.randn((N, K), dtype=torch.half, device=dev, generator=gen)
+        keep = W.abs().view(N, K // 4, 4).topk(2, dim=-1).indices
+        mask = torch.zeros((N, K // 4, 4), dtype=torch.bool, device=dev).scatter_(-1, keep, True)
+        Wc = torch._cslt_compress((W.view(N, K // 4, 4) * mask).view(N, K))
+        del W, mask, keep
+        for M in PREFILL_M:
+            A = torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
+            At = A.t()
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    torch._cslt_sparse_mm(Wc, At)
+                torch.cuda.synchronize(dev)
+                reps = max(3, min(args.steps, 20))
+                ev0.record(stream)
+                for _ in range(reps):
+                    torch._cslt_sparse_mm(Wc, At)
+                ev1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = ev0.elapsed_time(ev1) * 1e-3 / reps
+            fl = 2.0 * M * N * K
+            detail[f"M{M}_K{K}_N{N}"] = {"us": round(t * 1e6, 1), "TFLOP/s": round(fl / t / 1e12, 1)}
+            flops_total += fl
+            sec_total += t
+        del Wc
+    return flops_total / sec_total / 1e12, detail
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -433,6 +471,8 @@ def main():
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
                     help="decode: Llama-2-7B decode step (config 1, the headline); "
                          "prefill: compute-bound sweep (config 4)")
+    ap.add_argument("--no-comparator", action="store_true",
+                    help="prefill: skip the cuSPARSELt fp16 2:4 comparator")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers per step (32 = Llama-2-7B; fewer only for profiling)")
     args = ap.parse_args()
@@ -499,6 +539,15 @@ def main():
                               "unit": "TFLOP/s", "frac": round(value / (2 * dense), 4),
                               "peak_source": kind},
                     detail=detail)
+        if not args.no_comparator:
+            try:
+                cv, cdetail = bench_cusparselt(args, torch, dev)
+                line["comparator"] = {
+                    "library": "cuSPARSELt fp16 x fp16 2:4 (torch._cslt_sparse_mm), fp16 weights",
+                    "value": round(cv, 1), "unit": "TFLOP/s", "ours_over_library": round(value / cv, 3),
+                    "detail": cdetail}
+            except Exception as e:  # comparator only; never fails the bench line
+                line["comparator"] = {"library": "cuSPARSELt", "unavailable": str(e)[:200]}
         if rank == 0:
             print(json.dumps(line), flush=True)
         return
