@@ -22,7 +22,11 @@ import torch
 
 from . import _ext
 
-__all__ = ["mul_2_4", "scratch_bytes", "device_status", "Layer_2_4", "replace_linear"]
+__all__ = ["mul_2_4", "mul_2_4_epilogue", "ACTIVATIONS", "scratch_bytes", "device_status",
+           "Layer_2_4", "replace_linear"]
+
+# fused-epilogue activations (SM100_MARLIN_ACT_* of the C header)
+ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3}
 
 
 def _stream_ptr(dev: int) -> int:
@@ -65,7 +69,8 @@ def _raise_for(err: int, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize) 
 _HALF, _INT32, _INT16 = torch.half, torch.int32, torch.int16
 
 
-def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bits):
+def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bits, bias=None,
+         act=0):
     lib = _ext._lib or _ext.load()
     prob_n, prob_k = A.shape  # batch rows, input features
     prob_m = C.shape[1]       # output features
@@ -90,10 +95,20 @@ def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bit
         _check_cuda("C", C, _HALF, dev)
         _check_cuda("s", s, _HALF, dev)
         _check_cuda("workspace", workspace, _INT32, dev)
-    fn = lib.sm100_marlin_mul_2_4 if meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
-    err = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
-             prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
-             thread_m, sms, max_par)
+    if bias is None and act == 0:
+        fn = lib.sm100_marlin_mul_2_4 if meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
+        err = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
+                 prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
+                 thread_m, sms, max_par)
+    else:
+        if bias is not None:
+            _check_cuda("bias", bias, _HALF, dev)
+            if bias.numel() != prob_m:
+                raise RuntimeError(f"bias must have {prob_m} elements (one per output column)")
+        err = lib.sm100_marlin_mul_2_4_epilogue(
+            A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
+            prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
+            thread_m, sms, max_par, meta_bits, bias.data_ptr() if bias is not None else None, act)
     if err:
         _raise_for(err, prob_m, prob_n, prob_k, thread_k, thread_m, groupsize)
 
@@ -112,6 +127,26 @@ def mul_2_4(A, B, meta, C, s, workspace, thread_k=-1, thread_m=-1, sms=-1, max_p
     @max_par: as in the reference; only sizes the workspace requirement
     """
     _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, 4)
+
+
+def mul_2_4_epilogue(A, B, meta, C, s, workspace, bias=None, activation="none", thread_k=-1,
+                     thread_m=-1, sms=-1, max_par=16, meta_bits=4):
+    """``mul_2_4`` with a fused epilogue: ``C = act(A @ W + bias)``.
+
+    Not in the reference (its ``Layer_2_4`` is "without bias" and callers
+    apply bias and activation as separate ops); computed in fp32 and rounded
+    once to fp16 in the GEMM's store.
+    @bias: ``torch.half`` ``(m,)`` per output column, or None
+    @activation: one of ``ACTIVATIONS`` ("none", "relu", "silu", "gelu_tanh")
+    @meta_bits: 4 (int16 metadata) or 3 (``metadata_decode.pack`` output)
+    Other arguments as ``mul_2_4``.
+    """
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}")
+    if meta_bits not in (3, 4):
+        raise ValueError("meta_bits must be 3 or 4")
+    _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bits, bias,
+         ACTIVATIONS[activation])
 
 
 def scratch_bytes(prob_m: int, prob_n: int, prob_k: int, dev: int = 0, sms: int = -1) -> int:

@@ -29,6 +29,9 @@ SIGNATURES = {
     "sm100_marlin_mul_2_4_ex": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
                                          _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                                          _c_int, _vp, _size]),
+    "sm100_marlin_mul_2_4_epilogue": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
+                                               _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
+                                               _c_int, _vp, _c_int]),
     "sm100_marlin_mul_2_4_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp, _c_int, _c_int, _vp, _c_int, _c_int, _c_int,
                                               _c_int]),
@@ -57,6 +60,9 @@ OK = 0
 ERR_PROB_SHAPE = 1
 ERR_KERN_SHAPE = 2
 ERR_CUDA = 3
+ERR_ALIGNMENT = 4
+ERR_ARGUMENT = 5
+ERR_SCRATCH = 6
 
 
 def load(path: str = LIB_PATH):

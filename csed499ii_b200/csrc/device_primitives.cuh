@@ -101,6 +101,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
 }
 
 // ---------------------------------------------------------------------------
+// Fused epilogue: C = act(acc [* column scale] + bias), in fp32, rounded once
+// to fp16.  Activation codes match SM100_MARLIN_ACT_* of the C header.
+// ---------------------------------------------------------------------------
+enum : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGeluTanh = 3 };
+
+__device__ __forceinline__ float epilogue_act(float x, int act) {
+  if (act == kActRelu) return fmaxf(x, 0.f);
+  if (act == kActSilu) return x / (1.f + __expf(-x));
+  if (act == kActGeluTanh) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.f + tanhf(u));
+  }
+  return x;
+}
+
+// ---------------------------------------------------------------------------
 // GPU-scope counters for the split-K hand-over between CTAs.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {

@@ -66,6 +66,8 @@ struct GemmParams {
   long long units;      // n_tiles * kk_total / unit_kk
   unsigned long long* trace;  // optional per-CTA timestamps (SM100_MARLIN_TRACE builds)
   int pdl;              // launched with programmatic dependent launch
+  const half* bias;     // fused epilogue: fp16 bias per output column, or null
+  int act;              // fused epilogue: activation (kAct*)
   int prefetch;         // stages whose weights may be issued before griddepcontrol.wait
   // Fused all-gather of column-parallel shards (gather_world > 0): every C row
   // this launch computes is stored into each rank's gathered buffer (peer
@@ -676,6 +678,20 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
             if (!GROUPED) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) v[i] *= colscale[i];
+            }
+            if (p.bias != nullptr || p.act != kActNone) {
+              float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              if (p.bias != nullptr) {
+                const uint4 braw = *reinterpret_cast<const uint4*>(p.bias + n0);
+                const half2* bh = reinterpret_cast<const half2*>(&braw);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  bv[2 * i] = __low2float(bh[i]);
+                  bv[2 * i + 1] = __high2float(bh[i]);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[i] = epilogue_act(v[i] + bv[i], p.act);
             }
             uint4 o;
             half2* oh = reinterpret_cast<half2*>(&o);

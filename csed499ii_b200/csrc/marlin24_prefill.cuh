@@ -51,6 +51,8 @@ struct PrefillParams {
   CUtensorMap tm_c;     // C fp16, dims (N, M), box (128, 256)        (CTA-pair form only)
   const uint8_t* s;     // fp16 scales (per-column scaling in the epilogue)
   half* C;              // fp16 (M, N) row-major
+  const half* bias;     // fused epilogue: fp16 bias per output column, or null
+  int act;              // fused epilogue: activation (kAct*)
   int* status;          // device status word
   int M;
   int N;
@@ -364,6 +366,7 @@ __global__ void __launch_bounds__(PrefillCfg<BN, NG>::THREADS, 1)
       const int n = n_tile * 128 + feat;
       float cs = 1.f;
       if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n]);
+      const float col_bias = p.bias != nullptr ? __half2float(p.bias[n]) : 0.f;
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
 #pragma unroll 1
       for (int cb = grp; cb < BN / 32; cb += NG) {
@@ -374,7 +377,8 @@ __global__ void __launch_bounds__(PrefillCfg<BN, NG>::THREADS, 1)
         for (int j = 0; j < 32; ++j) {
           const int b = b0 + j;
           if (b < p.M)
-            p.C[static_cast<long long>(b) * p.N + n] = __float2half_rn(__uint_as_float(v[j]) * cs);
+            p.C[static_cast<long long>(b) * p.N + n] =
+                __float2half_rn(epilogue_act(__uint_as_float(v[j]) * cs + col_bias, p.act));
         }
       }
     } else if (ok && lane == 0) {

@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
       const int n = n_tile * 128 + feat;
       float cs = 1.f;
       if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n]);
+      const float col_bias = p.bias != nullptr ? __half2float(p.bias[n]) : 0.f;
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
 #pragma unroll 1
       for (int cb2 = grp; cb2 < BN / 32; cb2 += NG) {
@@ -312,7 +313,8 @@ __global__ void __launch_bounds__(PrefillSpCfg<BN, NG>::THREADS, 1)
         for (int j = 0; j < 32; ++j) {
           const int b = b0 + j;
           if (b < p.M)
-            p.C[static_cast<long long>(b) * p.N + n] = __float2half_rn(__uint_as_float(v[j]) * cs);
+            p.C[static_cast<long long>(b) * p.N + n] =
+                __float2half_rn(epilogue_act(__uint_as_float(v[j]) * cs + col_bias, p.act));
         }
       }
     } else if (ok && lane == 0) {
@@ -706,6 +708,7 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
       const int feat = 64 * (m2 >> 2) + 8 * (rr & 7) + (m2 & 3) + 4 * ((rr >> 3) & 1);
       float cs = 1.f;
       if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n_tile * 128 + feat]);
+      const float col_bias = p.bias != nullptr ? __half2float(p.bias[n_tile * 128 + feat]) : 0.f;
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
       const uint32_t c_col = ring_base + 2 * feat;
 #pragma unroll 1
@@ -715,7 +718,7 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           sts16(c_col + (cb2 * 32 + j) * 256,
-                __half_as_ushort(__float2half_rn(__uint_as_float(v[j]) * cs)));
+                __half_as_ushort(__float2half_rn(epilogue_act(__uint_as_float(v[j]) * cs + col_bias, p.act))));
       }
       fence_proxy_async_smem();
       stored = true;

@@ -567,10 +567,12 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
 // metadata): one 128 x BN output tile per CTA on the tcgen05 kernels.
 int mul_prefill(const void* A, const void* B, const void* meta, void* C, const void* s, int n_out,
                 int m_rows, int k_in, int groupsize, int dev, int sms, cudaStream_t stream,
-                int* status) {
+                int* status, const void* bias, int act) {
   PrefillParams p;
   p.s = static_cast<const uint8_t*>(s);
   p.C = static_cast<half*>(C);
+  p.bias = static_cast<const half*>(bias);
+  p.act = act;
   p.status = status;
   p.M = m_rows;
   p.N = n_out;
@@ -623,8 +625,11 @@ struct GatherArgs {
 int mul_impl(const void* A, const void* B, const void* meta, void* C, const void* s, int prob_m,
              int prob_n, int prob_k, void* workspace, int groupsize, int dev, void* stream_v,
              int thread_k, int thread_m, int sms, int max_par, int meta_bits, void* scratch,
-             size_t scratch_bytes, const GatherArgs* gather = nullptr) {
+             size_t scratch_bytes, const GatherArgs* gather = nullptr, const void* bias = nullptr,
+             int act = 0) {
   (void)max_par;
+  if (act < 0 || act > 3) return SM100_MARLIN_ERR_ARGUMENT;
+  if (bias != nullptr && !aligned16(bias)) return SM100_MARLIN_ERR_ALIGNMENT;
   if (prob_m < 0 || prob_n < 0 || prob_k < 0) return SM100_MARLIN_ERR_ARGUMENT;
   int rc = check_reference_shape(prob_m, prob_n, prob_k, groupsize, &thread_k, &thread_m);
   if (rc != SM100_MARLIN_OK) return rc;
@@ -650,7 +655,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
     if (e != cudaSuccess) return cuda_fail(e);
     return mul_prefill(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
-                       status);
+                       status, bias, act);
   }
 
   const int chunk_rows = prob_n < 64 ? prob_n : 64;
@@ -685,6 +690,8 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.trace = g_trace_buffer ? g_trace_buffer + g_trace_launch++ * kTraceLaunchWords : nullptr;
     p.pdl = pdl_enabled() ? 1 : 0;
     p.prefetch = prefetch_stages();
+    p.bias = static_cast<const half*>(bias);
+    p.act = act;
     p.gather_world = 0;
     p.gather_rank = 0;
     p.gather_seen = nullptr;
@@ -744,6 +751,17 @@ int sm100_marlin_mul_2_4_ex(const void* A, const void* B, const void* meta, void
   if (scratch == nullptr) return SM100_MARLIN_ERR_SCRATCH;
   return mul_impl(A, B, meta, C, s, prob_m, prob_n, prob_k, workspace, groupsize, dev, stream,
                   thread_k, thread_m, sms, max_par, meta_bits, scratch, scratch_bytes);
+}
+
+int sm100_marlin_mul_2_4_epilogue(const void* A, const void* B, const void* meta, void* C,
+                                  const void* s, int prob_m, int prob_n, int prob_k,
+                                  void* workspace, int groupsize, int dev, void* stream,
+                                  int thread_k, int thread_m, int sms, int max_par, int meta_bits,
+                                  const void* bias, int activation) {
+  if (meta_bits != 3 && meta_bits != 4) return SM100_MARLIN_ERR_ARGUMENT;
+  return mul_impl(A, B, meta, C, s, prob_m, prob_n, prob_k, workspace, groupsize, dev, stream,
+                  thread_k, thread_m, sms, max_par, meta_bits, nullptr, 0, nullptr, bias,
+                  activation);
 }
 
 int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta, void* C,

@@ -18,22 +18,31 @@ Differences a caller may notice:
   halves them in place);
 * only ``trans=True`` is accepted: ``trans=False`` selects the dense Marlin
   permutation, a layout the 2:4 kernel does not read.
+
+Extension (off by default, so the defaults match the reference): ``bias=True``
+adds a ``bias`` buffer (fp16, one per output feature, filled by ``pack`` from
+``linear.bias``) and ``activation`` names an activation; both are fused into
+the GEMM's store (:func:`csed499ii_b200.mul_2_4_epilogue`).
+``replace_linear(..., keep_bias=True)`` keeps each ``nn.Linear``'s bias.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 
-from . import _ext, mul_2_4
+from . import ACTIVATIONS, _ext, mul_2_4, mul_2_4_epilogue
 
 __all__ = ["Layer_2_4", "replace_linear"]
 
 
 class Layer_2_4(nn.Module):
-    """2:4-sparse INT4 (symmetric, grouped) linear layer without bias."""
+    """2:4-sparse INT4 (symmetric, grouped) linear layer; without bias unless
+    ``bias=True`` (an extension: bias and ``activation`` fused into the store)."""
 
-    def __init__(self, infeatures, outfeatures, groupsize=-1):
+    def __init__(self, infeatures, outfeatures, groupsize=-1, bias=False, activation="none"):
         super().__init__()
+        if activation not in ACTIVATIONS:
+            raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}")
         if groupsize not in [-1, 128]:
             raise ValueError("Only groupsize -1 and 128 are supported.")
         if infeatures % 128 != 0 or outfeatures % 256 != 0:
@@ -50,13 +59,22 @@ class Layer_2_4(nn.Module):
         self.register_buffer("s", torch.empty((self.k // groupsize, self.n), dtype=torch.half))
         self.register_buffer("workspace", torch.zeros(self.n // 128 * 16, dtype=torch.int32),
                              persistent=False)
+        self.activation = activation
+        if bias:
+            self.register_buffer("bias", torch.zeros(self.n, dtype=torch.half))
+        else:
+            self.bias = None
 
     def forward(self, A):
         C = torch.empty(A.shape[:-1] + (self.s.shape[1],), dtype=A.dtype, device=A.device)
         if self.workspace.device != A.device:
             self.workspace = self.workspace.to(A.device)
-        mul_2_4(A.view((-1, A.shape[-1])), self.B, self.meta, C.view((-1, C.shape[-1])), self.s,
-                self.workspace)
+        A2, C2 = A.view((-1, A.shape[-1])), C.view((-1, C.shape[-1]))
+        if self.bias is None and self.activation == "none":
+            mul_2_4(A2, self.B, self.meta, C2, self.s, self.workspace)
+        else:
+            mul_2_4_epilogue(A2, self.B, self.meta, C2, self.s, self.workspace, bias=self.bias,
+                             activation=self.activation)
         return C
 
     def pack(self, linear, scales, trans=True):
@@ -94,14 +112,21 @@ class Layer_2_4(nn.Module):
         self.B = B.to(self.B.device)
         self.meta = meta.to(self.meta.device)
         self.s = s_out.to(self.s.device)
+        if self.bias is not None and getattr(linear, "bias", None) is not None:
+            b = linear.bias.data.reshape(-1)
+            if b.numel() != self.n:
+                raise ValueError(f"bias must have {self.n} elements")
+            self.bias = b.to(device=self.bias.device, dtype=torch.half).contiguous()
 
 
-def replace_linear(module, name_filter=lambda n: True, groupsize=-1, name=""):
+def replace_linear(module, name_filter=lambda n: True, groupsize=-1, name="", keep_bias=False):
     """Recursively replace every ``torch.nn.Linear`` by an empty ``Layer_2_4``.
 
     Same traversal as the reference (``__init__.py:391-415``): attributes of
     ``module`` that are ``nn.Linear`` and pass ``name_filter`` (dotted name)
-    are replaced, then children are visited.
+    are replaced, then children are visited.  ``keep_bias=True`` (not in the
+    reference, which drops biases) gives layers with a bias buffer where the
+    ``nn.Linear`` has one.
     """
     if isinstance(module, Layer_2_4):
         return
@@ -109,7 +134,8 @@ def replace_linear(module, name_filter=lambda n: True, groupsize=-1, name=""):
         tmp = getattr(module, attr)
         name1 = name + "." + attr if name != "" else attr
         if isinstance(tmp, nn.Linear) and name_filter(name1):
-            setattr(module, attr, Layer_2_4(tmp.in_features, tmp.out_features, groupsize=groupsize))
+            setattr(module, attr, Layer_2_4(tmp.in_features, tmp.out_features, groupsize=groupsize,
+                                            bias=keep_bias and tmp.bias is not None))
     for name1, child in module.named_children():
         replace_linear(child, name_filter, groupsize=groupsize,
-                       name=name + "." + name1 if name != "" else name1)
+                       name=name + "." + name1 if name != "" else name1, keep_bias=keep_bias)

@@ -37,6 +37,12 @@ extern "C" {
 #define SM100_MARLIN_STATUS_FINISH_WAIT_TIMEOUT 4
 #define SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT 8
 
+/* Fused-epilogue activations (sm100_marlin_mul_2_4_epilogue). */
+#define SM100_MARLIN_ACT_NONE 0
+#define SM100_MARLIN_ACT_RELU 1
+#define SM100_MARLIN_ACT_SILU 2      /* x * sigmoid(x) */
+#define SM100_MARLIN_ACT_GELU_TANH 3 /* 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) */
+
 /*
  * C[prob_n, prob_m] (fp16, row-major) = A[prob_n, prob_k] (fp16, row-major)
  *     x dequant(B, meta, s)[prob_k, prob_m].
@@ -89,6 +95,23 @@ int sm100_marlin_mul_2_4_ex(const void* A, const void* B, const void* meta, void
                             int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
                             int dev, void* stream, int thread_k, int thread_m, int sms,
                             int max_par, int meta_bits, void* scratch, size_t scratch_bytes);
+
+/*
+ * mul_2_4 / mul_2_4_meta3 (`meta_bits` 4 or 3) with a fused epilogue:
+ * C = act(A . dequant(B, meta, s) + bias), computed in fp32 and rounded once
+ * to fp16.  `bias`: fp16 of prob_m (= N) values, 16-byte aligned, or NULL;
+ * `activation`: SM100_MARLIN_ACT_*.  No counterpart in the reference, whose
+ * Layer_2_4 is "without bias" (SRC/marlin/__init__.py:275) and whose callers
+ * apply bias and activation as separate PyTorch ops; this is the step after
+ * the GEMM fused into its store.  Errors as sm100_marlin_mul_2_4, plus
+ * SM100_MARLIN_ERR_ARGUMENT for an unknown activation or meta_bits and
+ * SM100_MARLIN_ERR_ALIGNMENT for an unaligned bias.
+ */
+int sm100_marlin_mul_2_4_epilogue(const void* A, const void* B, const void* meta, void* C,
+                                  const void* s, int prob_m, int prob_n, int prob_k,
+                                  void* workspace, int groupsize, int dev, void* stream,
+                                  int thread_k, int thread_m, int sms, int max_par, int meta_bits,
+                                  const void* bias, int activation);
 
 /*
  * sm100_marlin_mul_2_4 without any device allocation.  No counterpart in the
