@@ -489,7 +489,9 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
       : "memory");
 }
 
-template <int NG, bool GROUPED>
+// EPI: fused bias / activation compiled in (a separate instantiation; the
+// epilogue code cost the plain kernel 1-3 %).
+template <int NG, bool GROUPED, bool EPI>
 __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     marlin24_prefill_sp2_kernel(const __grid_constant__ PrefillParams p) {
   using Cfg = PrefillSp2Cfg<NG>;
@@ -708,7 +710,8 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
       const int feat = 64 * (m2 >> 2) + 8 * (rr & 7) + (m2 & 3) + 4 * ((rr >> 3) & 1);
       float cs = 1.f;
       if (!GROUPED) cs = __half2float(reinterpret_cast<const half*>(p.s)[n_tile * 128 + feat]);
-      const float col_bias = p.bias != nullptr ? __half2float(p.bias[n_tile * 128 + feat]) : 0.f;
+      const float col_bias =
+          EPI && p.bias != nullptr ? __half2float(p.bias[n_tile * 128 + feat]) : 0.f;
       const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
       const uint32_t c_col = ring_base + 2 * feat;
 #pragma unroll 1
@@ -718,7 +721,9 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           sts16(c_col + (cb2 * 32 + j) * 256,
-                __half_as_ushort(__float2half_rn(epilogue_act(__uint_as_float(v[j]) * cs + col_bias, p.act))));
+                __half_as_ushort(__float2half_rn(
+                    EPI ? epilogue_act(__uint_as_float(v[j]) * cs + col_bias, p.act)
+                        : __uint_as_float(v[j]) * cs)));
       }
       fence_proxy_async_smem();
       stored = true;

@@ -291,11 +291,11 @@ int encode_maps(GemmParams& p, const Plan& pl, const void* A, const void* B, con
   return SM100_MARLIN_OK;
 }
 
-template <int NC, int MB, int NH, bool META3, bool GROUPED>
+template <int NC, int MB, int NH, bool META3, bool GROUPED, bool EPI>
 int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
   using Cfg = DecodeCfg<NC, MB, META3>;
   static bool attr_set[64] = {};
-  auto kern = marlin24_decode_kernel<NC, MB, NH, META3, GROUPED>;
+  auto kern = marlin24_decode_kernel<NC, MB, NH, META3, GROUPED, EPI>;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -317,11 +317,11 @@ int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
-template <bool META3, bool GROUPED>
+template <bool META3, bool GROUPED, bool EPI>
 int dispatch_g(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
 #define SM100_CASE(NC_, MB_, NH_)                                            \
   if (pl.nc == NC_ && pl.mb == MB_ && pl.nh_last == NH_)                     \
-    return launch_one<NC_, MB_, NH_, META3, GROUPED>(p, pl.grid, dev, stream);
+    return launch_one<NC_, MB_, NH_, META3, GROUPED, EPI>(p, pl.grid, dev, stream);
 #define SM100_CASES_NC(NC_) \
   SM100_CASE(NC_, 1, 1)     \
   SM100_CASE(NC_, 1, 2)     \
@@ -337,8 +337,11 @@ int dispatch_g(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream
 
 template <bool META3>
 int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
-  return p.grouped ? dispatch_g<META3, true>(p, pl, dev, stream)
-                   : dispatch_g<META3, false>(p, pl, dev, stream);
+  if (p.bias != nullptr || p.act != kActNone)
+    return p.grouped ? dispatch_g<META3, true, true>(p, pl, dev, stream)
+                     : dispatch_g<META3, false, true>(p, pl, dev, stream);
+  return p.grouped ? dispatch_g<META3, true, false>(p, pl, dev, stream)
+                   : dispatch_g<META3, false, false>(p, pl, dev, stream);
 }
 
 // Reference shape rules (marlin_cuda_kernel_nm.cu:763-783,811-823).
@@ -454,11 +457,11 @@ int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) 
 }
 
 // CTA-pair form: 2-CTA clusters along the features, grid (N/128, M/256).
-template <int NG, bool GROUPED>
+template <int NG, bool GROUPED, bool EPI>
 int launch_prefill_sp2_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
   using Cfg = PrefillSp2Cfg<NG>;
   static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED>;
+  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED, EPI>;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -539,10 +542,13 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
     rc = encode_2d(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, p.C, N, static_cast<uint64_t>(p.M),
                    2 * N, 128, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
+    const bool epi = p.bias != nullptr || p.act != kActNone;
 #define SM100_PREFILL_SP2(NG_)                                                       \
   if (ng == NG_)                                                                     \
-    return p.grouped ? launch_prefill_sp2_cfg<NG_, true>(p, dev, stream)            \
-                     : launch_prefill_sp2_cfg<NG_, false>(p, dev, stream);
+    return p.grouped ? (epi ? launch_prefill_sp2_cfg<NG_, true, true>(p, dev, stream)   \
+                            : launch_prefill_sp2_cfg<NG_, true, false>(p, dev, stream)) \
+                     : (epi ? launch_prefill_sp2_cfg<NG_, false, true>(p, dev, stream)  \
+                            : launch_prefill_sp2_cfg<NG_, false, false>(p, dev, stream));
     SM100_PREFILL_SP2(1)
     SM100_PREFILL_SP2(2)
     SM100_PREFILL_SP2(4)
