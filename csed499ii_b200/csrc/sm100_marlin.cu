@@ -200,6 +200,12 @@ Plan make_plan(int n_out, int m_rows, int k_in, int sms) {
   const long long n_tiles = n_out / (64 * pl.nc);
   pl.units = n_tiles * (kk / pl.unit_kk);
   pl.grid = static_cast<int>(pl.units < sms ? pl.units : sms);
+  // Whole column tiles (no split-K) when they fit the SMs in one wave and a
+  // tile is at most 4 stages deep: the split-K hand-over costs ~3-4 us per
+  // call (per-CTA traces), more than the fewer SMs lose on short tiles.
+  // Measured at M = 16: K = N = 4096 5.87 vs 7.24 us; deeper tiles stream too
+  // slowly on fewer SMs (K = 11008, N = 4096: 11.0 vs 10.0 us).
+  if (n_tiles <= sms && kk <= 4 * pl.sk) pl.grid = static_cast<int>(n_tiles);
   // one fp32 partial tile (nc chunks x 16*mb rows x 64 columns) per CTA
   pl.scratch = static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 4096;
   return pl;
