@@ -46,3 +46,37 @@ def test_replace_linear_traversal_and_filter():
     assert isinstance(net.norm, nn.LayerNorm)
     replace_linear(net)  # idempotent on already replaced layers
     assert isinstance(net.q_proj, Layer_2_4)
+
+
+# Extension (not in the reference): a bias buffer and a fused activation.
+def test_bias_and_activation_options():
+    with pytest.raises(ValueError, match="activation"):
+        Layer_2_4(256, 256, activation="tanh")
+    plain = Layer_2_4(256, 256)
+    assert plain.bias is None and plain.activation == "none"
+    layer = Layer_2_4(256, 512, groupsize=128, bias=True, activation="silu")
+    assert layer.bias.shape == (512,) and layer.bias.dtype == torch.half
+    assert set(layer.state_dict()) == {"B", "meta", "s", "bias"}
+
+
+def test_replace_linear_keep_bias():
+    m = nn.Module()
+    m.a = nn.Linear(256, 512, bias=True)
+    m.b = nn.Linear(256, 512, bias=False)
+    replace_linear(m, keep_bias=True)
+    assert m.a.bias is not None and m.b.bias is None
+    m2 = nn.Module()
+    m2.a = nn.Linear(256, 512, bias=True)
+    replace_linear(m2)  # the reference's behaviour: biases are dropped
+    assert m2.a.bias is None
+
+
+def test_epilogue_argument_checks_before_the_gpu():
+    import csed499ii_b200 as marlin
+
+    assert marlin.ACTIVATIONS == {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3}
+    t = torch.zeros(1)
+    with pytest.raises(ValueError, match="activation"):
+        marlin.mul_2_4_epilogue(t, t, t, t, t, t, activation="swish")
+    with pytest.raises(ValueError, match="meta_bits"):
+        marlin.mul_2_4_epilogue(t, t, t, t, t, t, meta_bits=2)
