@@ -21,6 +21,7 @@
 #include "device_primitives.cuh"
 #include "marlin24_gemm.cuh"
 #include "marlin24_prefill.cuh"
+#include "marlin24_prefill_persistent.cuh"
 #include "marlin24_prefill_sparse.cuh"
 #include "packer.cuh"
 #include "meta3_codec.cuh"
@@ -489,6 +490,46 @@ int launch_prefill_sp2_cfg(const PrefillParams& p, int dev, cudaStream_t stream)
   return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
+// Persistent form: one 2-CTA cluster per SM pair, looping over tiles.
+template <int NG, bool GROUPED, bool EPI>
+int launch_prefill_sp2p_cfg(const PrefillParams& p, int dev, int sms, cudaStream_t stream) {
+  using Cfg = PrefillSp2pCfg<NG>;
+  static bool attr_set[64] = {};
+  auto kern = marlin24_prefill_sp2p_kernel<NG, GROUPED, EPI>;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int tiles = (p.N / 256) * ((p.M + 255) / 256);
+  const int max_clusters = sms / 2 > 0 ? sms / 2 : 1;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+// SM100_MARLIN_PREFILL_PERSISTENT=1 runs the CTA-pair prefill persistently
+// (tuning / comparison knob).
+bool prefill_persistent_enabled() {
+  static const bool v = [] {
+    const char* e = std::getenv("SM100_MARLIN_PREFILL_PERSISTENT");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 // SM100_MARLIN_PREFILL_PAIR=0 keeps 256-row prefill tiles on one CTA
 // (tuning / comparison knob; default: CTA pairs).
 bool prefill_pair_enabled() {
@@ -549,6 +590,11 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
                    2 * N, 128, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const bool epi = p.bias != nullptr || p.act != kActNone;
+    if (prefill_persistent_enabled() && ng == 4)
+      return p.grouped ? (epi ? launch_prefill_sp2p_cfg<4, true, true>(p, dev, sms, stream)
+                              : launch_prefill_sp2p_cfg<4, true, false>(p, dev, sms, stream))
+                       : (epi ? launch_prefill_sp2p_cfg<4, false, true>(p, dev, sms, stream)
+                              : launch_prefill_sp2p_cfg<4, false, false>(p, dev, sms, stream));
 #define SM100_PREFILL_SP2(NG_)                                                       \
   if (ng == NG_)                                                                     \
     return p.grouped ? (epi ? launch_prefill_sp2_cfg<NG_, true, true>(p, dev, stream)   \
@@ -662,7 +708,16 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   if (sms <= 0) return SM100_MARLIN_ERR_ARGUMENT;
 
   if (gather && prob_n > 64) return SM100_MARLIN_ERR_ARGUMENT;
-  if (meta_bits == 4 && prob_n > prefill_min_rows() && prob_m % 128 == 0 && prob_k % 64 == 0) {
+  // The tcgen05 prefill kernels take batches above 64 rows, and 33-64 rows
+  // where the CTA-pair kernel's tiles fit one wave and K <= 8192: there the
+  // mma.sync decode kernel (4 row blocks) is compute-bound (Llama-7B at
+  // M = 64: 32.4 / 23.0 us for (4096, 12288) / (4096, 4096) against 20.7 /
+  // 20.4 on the pair kernel; longer K or two waves stay on decode).
+  const bool mid_batch_pair = !gather && prob_n > 32 && prob_m % 256 == 0 &&
+                              prob_k % 128 == 0 && prob_k <= 8192 && prob_m / 128 <= sms &&
+                              prefill_min_rows() == 64 && prefill_pair_enabled();
+  if (meta_bits == 4 && prob_m % 128 == 0 && prob_k % 64 == 0 &&
+      (prob_n > prefill_min_rows() || mid_batch_pair)) {
     int* status = nullptr;
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
     if (e != cudaSuccess) return cuda_fail(e);

@@ -256,6 +256,72 @@ def test_prefill_single_cta():
         assert finite and rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (K, N, M, g, sms, rel_mae, rel_fro)
 
 
+_PERSISTENT_SCRIPT = r"""
+import json, sys
+import numpy as np, torch
+import torch.nn.functional as F
+sys.path.insert(0, sys.argv[1])
+from problems import activations, errors, quantized_problem, random_packed_problem
+import csed499ii_b200 as m
+torch.backends.cuda.matmul.allow_tf32 = False
+out = []
+dev = "cuda:0"
+# (K, N, M, g, sms, epilogue): a small `sms` gives few clusters, so each
+# cluster loops over many tiles; ragged batches; both scale modes
+for K, N, M, g, sms, epi in [(1024, 2048, 1000, 128, 8, False), (512, 1536, 300, -1, 4, False),
+                             (2048, 512, 257, 128, 148, False), (1024, 1024, 700, 128, 6, True),
+                             (4096, 4096, 2048, 128, 148, False)]:
+    if g == -1:
+        W, B, s, meta = quantized_problem(N, K, -1, seed=K + N)
+    else:
+        W, B, s, meta = random_packed_problem(N, K, 128, seed=K + N + M)
+    A = activations(M, K, seed=M + 5)
+    C = torch.zeros((M, N), dtype=torch.half, device=dev)
+    ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
+    args = (torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev), torch.from_numpy(meta).to(dev),
+            C, torch.from_numpy(s).to(dev), ws)
+    ref = torch.from_numpy(A).to(dev).float() @ torch.from_numpy(W).to(dev).float()
+    if epi:
+        bias = torch.randn((N,), dtype=torch.half, device=dev)
+        m.mul_2_4_epilogue(*args, bias=bias, activation="silu", sms=sms)
+        ref = F.silu(ref + bias.float())
+    else:
+        m.mul_2_4(*args, -1, -1, sms, 16)
+    torch.cuda.synchronize()
+    rel_mae, rel_fro, _ = errors(C, ref)
+    C2 = C.clone()
+    if not epi:
+        m.mul_2_4(*args, -1, -1, sms, 16)
+        torch.cuda.synchronize()
+    out.append([K, N, M, g, sms, epi, rel_mae, rel_fro, bool(torch.isfinite(C).all()),
+                bool(torch.equal(C, C2))])
+out.append(m.device_status(0))
+print(json.dumps(out))
+"""
+
+
+# The persistent CTA-pair form (SM100_MARLIN_PREFILL_PERSISTENT=1, read once
+# per process, hence the child process): clusters loop over tiles; results
+# must match the oracle and repeat bit for bit.
+def test_prefill_persistent_pairs():
+    import json
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, SM100_MARLIN_PREFILL_PERSISTENT="1",
+               PYTHONPATH=os.pathsep.join([os.path.dirname(here), os.path.join(os.path.dirname(here), "oracle"),
+                                           os.environ.get("PYTHONPATH", "")]))
+    res = subprocess.run([sys.executable, "-c", _PERSISTENT_SCRIPT, here], env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    assert out[-1] == 0, f"device status {out[-1]}"
+    for K, N, M, g, sms, epi, rel_mae, rel_fro, finite, same in out[:-1]:
+        assert finite and same and rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (
+            K, N, M, g, sms, epi, rel_mae, rel_fro, same)
+
+
 def test_prefill_pair_deterministic():
     W, B, s, meta = random_packed_problem(2048, 1024, 128, seed=14)
     A = activations(384, 1024, seed=15)
