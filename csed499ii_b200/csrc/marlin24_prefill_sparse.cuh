@@ -591,36 +591,35 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
       const uint64_t bd0 = umma_desc_sw128_k(ring_base + Cfg::OFF_ACT);
       const uint32_t ready0 = smem_addr(aready_bar);
       const uint32_t empty0 = smem_addr(empty_bar);
-      uint64_t ad = ad0, bd = bd0;
-      uint32_t e = tmem_e, slot = 0, parity = 0;
-      for (int ks = 0; ks < ksteps; ++ks) {
-        // one wait per step: activations landed and both CTAs' tiles dequantised
-        const bool ok = mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {
-          if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          // four MMAs of K = 32: 32 compressed bytes of each 128-byte weight
-          // row; 64 bytes of each 128-byte activation row, two atoms
-          umma_sp_f16_pair(tmem, ad, bd, e, idesc, ks ? 1u : 0u);
-          umma_sp_f16_pair(tmem, ad + 2, bd + 4, e + 4, idesc, 1u);
-          umma_sp_f16_pair(tmem, ad + 4, bd + kAtomDesc, e + 8, idesc, 1u);
-          umma_sp_f16_pair(tmem, ad + 6, bd + kAtomDesc + 4, e + 12, idesc, 1u);
-          umma_commit_pair(empty0 + 8 * slot);
-        }
-        __syncwarp();
-        if (++slot == D) {
-          slot = 0;
-          parity ^= 1;
-          ad = ad0;
-          bd = bd0;
-          e = tmem_e;
-        } else {
-          ad += kStageDesc;
-          bd += kStageDesc;
-          e += Cfg::META_COLS;
+      uint32_t parity = 0;
+      bool ok = true;
+      // The loop runs a ring's worth of steps per iteration, so slot numbers
+      // and descriptor offsets are compile-time constants.
+      for (int ks0 = 0; ks0 < ksteps && ok; ks0 += D, parity ^= 1) {
+#pragma unroll
+        for (int slot = 0; slot < D; ++slot) {
+          const int ks = ks0 + slot;
+          if (ks >= ksteps) break;
+          // one wait per step: activations landed and both CTAs' tiles dequantised
+          ok = mbar_wait_bounded(ready0 + 8 * slot, parity, abort_flag);
+          if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            // four MMAs of K = 32: 32 compressed bytes of each 128-byte weight
+            // row; 64 bytes of each 128-byte activation row, two atoms
+            const uint64_t ad = ad0 + slot * kStageDesc, bd = bd0 + slot * kStageDesc;
+            const uint32_t e = tmem_e + slot * Cfg::META_COLS;
+            umma_sp_f16_pair(tmem, ad, bd, e, idesc, ks ? 1u : 0u);
+            umma_sp_f16_pair(tmem, ad + 2, bd + 4, e + 4, idesc, 1u);
+            umma_sp_f16_pair(tmem, ad + 4, bd + kAtomDesc, e + 8, idesc, 1u);
+            umma_sp_f16_pair(tmem, ad + 6, bd + kAtomDesc + 4, e + 12, idesc, 1u);
+            umma_commit_pair(empty0 + 8 * slot);
+          }
+          __syncwarp();
         }
       }
       if (lane == 0) umma_commit_pair(smem_addr(acc_bar));
