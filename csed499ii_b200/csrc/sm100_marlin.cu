@@ -12,8 +12,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <map>
 #include <mutex>
+#include <unordered_map>
 #include <string>
 #include <utility>
 
@@ -152,9 +154,40 @@ int noalloc_scratch(int dev, void** out) {
   return SM100_MARLIN_OK;
 }
 
+// Per-call host costs are on the eager path's critical path (an eager
+// decode step issues ~10 us of host work per ~10 us GEMM), so what never
+// changes between calls is looked up once: the SM count, the address of the
+// device status word, and encoded tensor maps.
 int device_sms(int dev, int* sms) {
+  static std::atomic<int> cache[64] = {};
+  if (dev >= 0 && dev < 64) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) {
+      *sms = v;
+      return SM100_MARLIN_OK;
+    }
+  }
   cudaError_t e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev >= 0 && dev < 64) cache[dev].store(*sms, std::memory_order_relaxed);
+  return SM100_MARLIN_OK;
+}
+
+// Device address of g_device_status on the current device (looked up once
+// per device; the caller has made `dev` current).
+int device_status_ptr(int dev, int** out) {
+  static std::atomic<int*> cache[64] = {};
+  if (dev >= 0 && dev < 64) {
+    int* v = cache[dev].load(std::memory_order_acquire);
+    if (v != nullptr) {
+      *out = v;
+      return SM100_MARLIN_OK;
+    }
+  }
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_device_status);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev >= 0 && dev < 64) cache[dev].store(*out, std::memory_order_release);
+  return SM100_MARLIN_OK;
 }
 
 // Column-tile width (in 64-column chunks).  Wider tiles re-read the
@@ -228,9 +261,65 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// An encoded tensor map is a pure function of its arguments, so a cache keyed
+// on all of them is always valid (a freed and reused address with the same
+// dims and box encodes to the same map).  Cleared when it grows past 4096.
+struct TmapKey {
+  uint64_t w[12];
+  bool operator==(const TmapKey& o) const { return std::memcmp(w, o.w, sizeof(w)) == 0; }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    uint64_t h = 1469598103934665603ull;
+    for (uint64_t x : k.w) h = (h ^ x) * 1099511628211ull;
+    return static_cast<size_t>(h);
+  }
+};
+struct TmapCache {
+  std::mutex mu;
+  std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> maps;
+};
+TmapCache& tmap_cache() {
+  static TmapCache c;
+  return c;
+}
+
+int encode_nd_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                       CUtensorMapSwizzle swizzle);
+
 int encode_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
               CUtensorMapSwizzle swizzle) {
+  TmapKey key = {};
+  key.w[0] = static_cast<uint64_t>(dtype) | (static_cast<uint64_t>(rank) << 16) |
+             (static_cast<uint64_t>(swizzle) << 32);
+  key.w[1] = reinterpret_cast<uint64_t>(base);
+  for (int i = 0; i < rank; ++i) {
+    key.w[2 + i] = dims[i];
+    key.w[5 + i] = box[i];
+    if (i + 1 < rank) key.w[8 + i] = strides_bytes[i];
+  }
+  TmapCache& c = tmap_cache();
+  {
+    std::lock_guard<std::mutex> lock(c.mu);
+    auto it = c.maps.find(key);
+    if (it != c.maps.end()) {
+      *map = it->second;
+      return SM100_MARLIN_OK;
+    }
+  }
+  const int rc = encode_nd_uncached(map, dtype, base, rank, dims, strides_bytes, box, swizzle);
+  if (rc != SM100_MARLIN_OK) return rc;
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (c.maps.size() >= 4096) c.maps.clear();
+  c.maps.emplace(key, *map);
+  return SM100_MARLIN_OK;
+}
+
+int encode_nd_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank,
+                       const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                       CUtensorMapSwizzle swizzle) {
   auto enc = tensor_map_encoder();
   if (!enc) {
     t_last_cuda_error = "cuTensorMapEncodeTiled unavailable";
@@ -719,8 +808,8 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   if (meta_bits == 4 && prob_m % 128 == 0 && prob_k % 64 == 0 &&
       (prob_n > prefill_min_rows() || mid_batch_pair)) {
     int* status = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
-    if (e != cudaSuccess) return cuda_fail(e);
+    rc = device_status_ptr(dev, &status);
+    if (rc != SM100_MARLIN_OK) return rc;
     return mul_prefill(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
                        status, bias, act);
   }
@@ -734,8 +823,8 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     return SM100_MARLIN_ERR_SCRATCH;
   }
   int* status = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_device_status);
-  if (e != cudaSuccess) return cuda_fail(e);
+  rc = device_status_ptr(dev, &status);
+  if (rc != SM100_MARLIN_OK) return rc;
 
   for (int r0 = 0; r0 < prob_n; r0 += 64) {
     const int rows = (prob_n - r0) < 64 ? (prob_n - r0) : 64;
