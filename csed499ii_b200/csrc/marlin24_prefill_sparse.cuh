@@ -491,7 +491,11 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 
 // EPI: fused bias / activation compiled in (a separate instantiation; the
 // epilogue code cost the plain kernel 1-3 %).
-template <int NG, bool GROUPED, bool EPI>
+// META3: 3-bit metadata (kernel_experiments/sparse_marlin/metadata_decode):
+// per 32-K row and 64-feature chunk 48 words instead of 64; each dequantising
+// thread decodes its one 4-bit word from two of them before the copy into
+// tensor memory, so the MMAs are unchanged.
+template <int NG, bool GROUPED, bool EPI, bool META3 = false>
 __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     marlin24_prefill_sp2_kernel(const __grid_constant__ PrefillParams p) {
   using Cfg = PrefillSp2Cfg<NG>;
@@ -554,7 +558,8 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     // the rest of its warp waits at the CTA barrier runs slower).
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
-    const uint32_t txw = Cfg::TX_W + (GROUPED ? 256 : 0);
+    // packed codes 4 x 1 KB, metadata 4 x 512 B (4-bit) or 4 x 384 B (3-bit)
+    const uint32_t txw = 4096 + (META3 ? 1536 : 2048) + (GROUPED ? 256 : 0);
     const int act_row = m_tile * 256 + static_cast<int>(rank) * Cfg::ROWS;
     for (int ks = 0; ks < ksteps; ++ks) {
       const int slot = ks % D;
@@ -569,7 +574,8 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
         const uint32_t wfull = smem_addr(&wfull_bar[slot]);
         mbar_arrive_expect_tx(wfull, txw);
         tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 4, wfull, pol_stream);
-        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * 64, ks * 4, wfull, pol_stream);
+        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * (META3 ? 48 : 64), ks * 4, wfull,
+                    pol_stream);
         if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks, wfull, pol_keep);
         // both CTAs' activation halves count on the even CTA's ready barrier
         const uint32_t ready = smem_addr(&aready_bar[slot]);
@@ -633,6 +639,10 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     const int g = lane >> 2, t = lane & 3;
     const uint32_t m_word = (quarter >> 1) * 256 +
                             4 * (32 * (quarter & 1) + 4 * (lane & 7) + 2 * (lane >> 4) + ((lane >> 3) & 1));
+    // 3-bit: word l = (4-bit word) mod 32 of the chunk's 48-word block
+    const uint32_t m3_l = 4 * (lane & 7) + 2 * (lane >> 4) + ((lane >> 3) & 1);
+    const uint32_t m3_word = (quarter >> 1) * 192 + 4 * m3_l;
+    const bool m3_upper = m3_l >= 16;
     const uint32_t e_lane = tmem_e + (static_cast<uint32_t>(32 * quarter) << 16);
     const uint32_t ready_own = smem_addr(aready_bar);
     bool ok = true;
@@ -647,8 +657,23 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
       const uint32_t st = ring_base + slot * Cfg::STAGE;
       // metadata of the four MMAs into this warp's lanes of the stage's slots
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        tmem_st32(e_lane + slot * Cfg::META_COLS + 4 * kk, lds32(st + Cfg::OFF_M + kk * 512 + m_word));
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t mw;
+        if constexpr (META3) {
+          // 4-bit word w of chunk quarter/2 (w >= 32 exactly in odd quarters)
+          // is the high (w < 32) or low (w >= 32) decode of 3-bit words
+          // l = w mod 32 and l + 16 of the chunk's 48 (see meta3_pair_decode)
+          const uint32_t a = lds32(st + Cfg::OFF_M + kk * 384 + m3_word);
+          const uint32_t b = lds32(st + Cfg::OFF_M + kk * 384 + m3_word + 64);
+          if (quarter & 1)
+            mw = decode24_low(m3_upper ? (b >> 8) : __funnelshift_r(a, b, 24));
+          else
+            mw = decode24_high(m3_upper ? __funnelshift_r(a, b, 16) : a);
+        } else {
+          mw = lds32(st + Cfg::OFF_M + kk * 512 + m_word);
+        }
+        tmem_st32(e_lane + slot * Cfg::META_COLS + 4 * kk, mw);
+      }
       // compressed weights of 32-K row r, both 64-feature chunks
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {

@@ -553,11 +553,11 @@ int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) 
 }
 
 // CTA-pair form: 2-CTA clusters along the features, grid (N/128, M/256).
-template <int NG, bool GROUPED, bool EPI>
+template <int NG, bool GROUPED, bool EPI, bool META3 = false>
 int launch_prefill_sp2_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
   using Cfg = PrefillSp2Cfg<NG>;
   static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED, EPI>;
+  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED, EPI, META3>;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return cuda_fail(e);
@@ -631,7 +631,7 @@ bool prefill_pair_enabled() {
 
 // The structured-sparse form: K steps of 64 (as the dense form).
 int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const void* meta,
-                       const void* s, int dev, int sms, cudaStream_t stream) {
+                       const void* s, int dev, int sms, cudaStream_t stream, int meta_bits) {
   const uint64_t N = p.N, K = p.K;
   const int n_tiles = p.N / 128;
   // CTA pairs (256 features x 256 rows, 128-K steps) whenever the pair's 256
@@ -641,6 +641,8 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   // quarter of the SMs idle (the 128-row tile is ~2x slower per CTA).
   int bn = prefill_forced_bn();
   const bool pair = p.N % 256 == 0 && prefill_pair_enabled() && bn != 128;
+  // 3-bit metadata: CTA-pair kernel only (the caller routes nothing else here)
+  if (meta_bits == 3 && !pair) return SM100_MARLIN_ERR_KERN_SHAPE;
   if (bn == 0)
     bn = pair || (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
   int rc;
@@ -662,8 +664,12 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, rows32,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, rows32,
-                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (meta_bits == 3)  // 48 words per 64 features and 32-K row: 3N/8 u64 per row
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, 3 * N / 8, K / 32, 3 * N, 48,
+                   rows32, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64,
+                   rows32, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   if (p.grouped) {
     rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, 1,
@@ -679,6 +685,11 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
                    2 * N, 128, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const bool epi = p.bias != nullptr || p.act != kActNone;
+    if (meta_bits == 3)
+      return p.grouped ? (epi ? launch_prefill_sp2_cfg<4, true, true, true>(p, dev, stream)
+                              : launch_prefill_sp2_cfg<4, true, false, true>(p, dev, stream))
+                       : (epi ? launch_prefill_sp2_cfg<4, false, true, true>(p, dev, stream)
+                              : launch_prefill_sp2_cfg<4, false, false, true>(p, dev, stream));
     if (prefill_persistent_enabled() && ng == 4)
       return p.grouped ? (epi ? launch_prefill_sp2p_cfg<4, true, true>(p, dev, sms, stream)
                               : launch_prefill_sp2p_cfg<4, true, false>(p, dev, sms, stream))
@@ -714,7 +725,7 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
 // metadata): one 128 x BN output tile per CTA on the tcgen05 kernels.
 int mul_prefill(const void* A, const void* B, const void* meta, void* C, const void* s, int n_out,
                 int m_rows, int k_in, int groupsize, int dev, int sms, cudaStream_t stream,
-                int* status, const void* bias, int act) {
+                int* status, const void* bias, int act, int meta_bits) {
   PrefillParams p;
   p.s = static_cast<const uint8_t*>(s);
   p.C = static_cast<half*>(C);
@@ -725,8 +736,8 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   p.N = n_out;
   p.K = k_in;
   p.grouped = groupsize != -1 ? 1 : 0;
-  if (prefill_sparse_enabled() && k_in % 128 == 0)
-    return mul_prefill_sparse(p, A, B, meta, s, dev, sms, stream);
+  if (meta_bits == 3 || (prefill_sparse_enabled() && k_in % 128 == 0))
+    return mul_prefill_sparse(p, A, B, meta, s, dev, sms, stream, meta_bits);
   const int n_tiles = n_out / 128;
   const int bn = (m_rows >= 256 && static_cast<long long>(n_tiles) * ((m_rows + 255) / 256) >= sms)
                      ? 256 : 128;
@@ -805,13 +816,18 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   const bool mid_batch_pair = !gather && prob_n > 32 && prob_m % 256 == 0 &&
                               prob_k % 128 == 0 && prob_k <= 8192 && prob_m / 128 <= sms &&
                               prefill_min_rows() == 64 && prefill_pair_enabled();
-  if (meta_bits == 4 && prob_m % 128 == 0 && prob_k % 64 == 0 &&
+  // 3-bit metadata: the CTA-pair kernel decodes it (N % 256, K % 128);
+  // other shapes stay on the decode kernel in 64-row chunks.
+  const bool pair_meta3 = meta_bits == 3 && prob_m % 256 == 0 && prob_k % 128 == 0 &&
+                          prefill_pair_enabled() && prefill_sparse_enabled() &&
+                          prefill_forced_bn() != 128;
+  if (((meta_bits == 4 && prob_m % 128 == 0 && prob_k % 64 == 0) || pair_meta3) &&
       (prob_n > prefill_min_rows() || mid_batch_pair)) {
     int* status = nullptr;
     rc = device_status_ptr(dev, &status);
     if (rc != SM100_MARLIN_OK) return rc;
     return mul_prefill(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
-                       status, bias, act);
+                       status, bias, act, meta_bits);
   }
 
   const int chunk_rows = prob_n < 64 ? prob_n : 64;

@@ -107,6 +107,25 @@ def test_meta3_llama7b_shapes(K, N, M):
     assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL
 
 
+# Batches above 64 rows, and 33-64 rows where the pair kernel's tiles fit one
+# wave, run the CTA-pair tensor-core kernel, whose dequantising warps decode
+# the 3-bit metadata: bit-identical to the same kernel on 4-bit metadata, and
+# within the tolerances of the oracle; ragged batches, both scale modes.
+@pytest.mark.parametrize("K,N,M,g", [(1024, 1024, 300, 128), (4096, 4096, 64, 128),
+                                     (2048, 1536, 1000, -1), (4096, 11008, 200, 128)])
+def test_meta3_prefill_pair_kernel(K, N, M, g):
+    if g == -1:
+        W, B, s, meta = quantized_problem(N, K, -1, seed=K + N)
+    else:
+        W, B, s, meta = random_packed_problem(N, K, 128, seed=K + N + M)
+    A = activations(M, K, seed=M + 6)
+    c4 = _gemm(A, B, meta, s, N, False)
+    c3 = _gemm(A, B, meta, s, N, True)
+    assert torch.equal(c3, c4)
+    rel_mae, rel_fro, _ = errors(c3, torch.from_numpy(A).to(DEV).float() @ torch.from_numpy(W).to(DEV).float())
+    assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL
+
+
 def test_meta3_shape_checks():
     from csed499ii_b200 import metadata_decode as md
 
