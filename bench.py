@@ -387,17 +387,17 @@ def bench_prefill(args, torch, dev):
     detail, flops_total, sec_total = {}, 0.0, 0.0
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.Stream(device=dev)
+    fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
     for (K, N) in PREFILL_SHAPES:
-        B, meta, s = make_layer(torch, K, N, dev, gen, 4)
+        B, meta, s = make_layer(torch, K, N, dev, gen, args.meta_bits)
         ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
         for M in PREFILL_M:
             A = torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
             C = torch.empty((M, N), dtype=torch.half, device=dev)
 
             def call():
-                rc = lib.sm100_marlin_mul_2_4(A.data_ptr(), B.data_ptr(), meta.data_ptr(),
-                                              C.data_ptr(), s.data_ptr(), N, M, K, ws.data_ptr(),
-                                              GROUP // 2, devi, stream.cuda_stream, -1, -1, -1, 16)
+                rc = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), N, M,
+                        K, ws.data_ptr(), GROUP // 2, devi, stream.cuda_stream, -1, -1, -1, 16)
                 if rc != 0:
                     raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
             for _ in range(args.warmup):
@@ -530,11 +530,13 @@ def main():
             kind = "derived: 2 x measured dense bf16 (MEASURED_PEAKS.json)"
         except Exception:
             dense, kind = 1590.0, "derived: 2 x fallback dense"
-        line = dict(metric="2:4 W4A16 GEMM dense-equivalent TFLOP/s (prefill sweep, config 4)",
+        line = dict(metric="2:4 W4A16 GEMM dense-equivalent TFLOP/s (prefill sweep, config 4)"
+                    + ("" if args.meta_bits == 4 else ", 3-bit metadata"),
                     value=round(value, 1), unit="TFLOP/s", n_gpus=1, steps=args.steps,
                     warmup=args.warmup, higher_is_better=True, scaling="weak", vs_baseline=None,
                     dtype="f16", data="synthetic (random packed INT4 codes, legal 2:4 metadata)",
-                    config={"workload": f"M in {PREFILL_M} x (K,N) in {PREFILL_SHAPES}, g128"},
+                    config={"workload": f"M in {PREFILL_M} x (K,N) in {PREFILL_SHAPES}, g128",
+                            "meta_bits": args.meta_bits},
                     roofline={"bound": "tensor", "achieved": round(value, 1), "peak": 2 * dense,
                               "unit": "TFLOP/s", "frac": round(value / (2 * dense), 4),
                               "peak_source": kind},
