@@ -95,16 +95,22 @@ def _mul(A, B, meta, C, s, workspace, thread_k, thread_m, sms, max_par, meta_bit
         _check_cuda("C", C, _HALF, dev)
         _check_cuda("s", s, _HALF, dev)
         _check_cuda("workspace", workspace, _INT32, dev)
-    if bias is None and act == 0:
+    fc = _ext._fast if _ext._fast_tried else _ext.fast()
+    if bias is not None:
+        _check_cuda("bias", bias, _HALF, dev)
+        if bias.numel() != prob_m:
+            raise RuntimeError(f"bias must have {prob_m} elements (one per output column)")
+    if fc is not None:
+        err = fc.mul(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
+                     prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
+                     thread_m, sms, max_par, meta_bits, bias.data_ptr() if bias is not None else 0,
+                     act)
+    elif bias is None and act == 0:
         fn = lib.sm100_marlin_mul_2_4 if meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
         err = fn(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
                  prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,
                  thread_m, sms, max_par)
     else:
-        if bias is not None:
-            _check_cuda("bias", bias, _HALF, dev)
-            if bias.numel() != prob_m:
-                raise RuntimeError(f"bias must have {prob_m} elements (one per output column)")
         err = lib.sm100_marlin_mul_2_4_epilogue(
             A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(), s.data_ptr(), prob_m,
             prob_n, prob_k, workspace.data_ptr(), groupsize, dev, _stream_ptr(dev), thread_k,

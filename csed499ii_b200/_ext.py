@@ -65,6 +65,26 @@ ERR_ARGUMENT = 5
 ERR_SCRATCH = 6
 
 
+_fast = None
+_fast_tried = False
+
+
+def fast():
+    """The CPython binding of the GEMM entry points (``_fastcall``, built by
+    ``build.build_fastcall``), or None when it has not been built: callers
+    then use the ctypes table, which reaches the same C ABI."""
+    global _fast, _fast_tried
+    if not _fast_tried:
+        _fast_tried = True
+        load()  # the binding links the library: make sure it is present first
+        try:
+            from . import _fastcall
+            _fast = _fastcall
+        except ImportError:
+            _fast = None
+    return _fast
+
+
 def load(path: str = LIB_PATH):
     """Load (once) and return the library; raise if it is not built."""
     global _lib

@@ -10,6 +10,7 @@ from __future__ import annotations
 import os
 import shutil
 import subprocess
+import sysconfig
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -77,5 +78,32 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False,
     return out
 
 
+FAST_NAME = "_fastcall" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so")
+FAST_PATH = os.path.join(HERE, FAST_NAME)
+
+
+def build_fastcall(force: bool = False) -> str:
+    """Compile the CPython binding (csrc/pybind_fast.c) next to the package;
+    it links the C-ABI library from _lib/ (rpath $ORIGIN/_lib)."""
+    src = os.path.join(CSRC, "pybind_fast.c")
+    hdr = os.path.join(ROOT, "include", "sm100_marlin.h")
+    if (not force and os.path.exists(FAST_PATH)
+            and os.path.getmtime(FAST_PATH) >= max(os.path.getmtime(src), os.path.getmtime(hdr),
+                                                   os.path.getmtime(LIB_PATH))):
+        return FAST_PATH
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("no C compiler for the CPython binding")
+    tmp = FAST_PATH + ".tmp"
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], src, "-o", tmp,
+           "-L", LIB_DIR, "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN/_lib"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("building the CPython binding failed:\n" + res.stdout + res.stderr)
+    os.replace(tmp, FAST_PATH)
+    return FAST_PATH
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv)
+    build_fastcall(force="--force" in sys.argv)
