@@ -86,9 +86,11 @@ struct GemmParams {
 // Per-CTA timeline written when the library is built with
 // -DSM100_MARLIN_TRACE=1 (off by default): %globaltimer at kernel entry, first
 // TMA issue, first stage consumed, last stage consumed, end of epilogue, the
-// number of stages and fixups of the CTA, and the time its consumers returned
-// from the programmatic-launch wait.
-constexpr int kTraceWords = 8;
+// number of stages and fixups of the CTA, the time its consumers returned
+// from the programmatic-launch wait, and inside the epilogue of the last
+// segment: [11] past the dependency wait, [8] warps reduced, [9] finisher
+// partials ready, [10] C stores issued (warp 0 of chunk 0).
+constexpr int kTraceWords = 16;
 // CTA 0 additionally records per-stage SM clock cycles (clock64, cheap to
 // read) after the per-CTA words: [stage][0] producer issue, [1..3] consumer
 // warp 0 wait start / data ready / done, [4..6] the same for the last
@@ -551,6 +553,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       epi_waited = true;
       if (trace && threadIdx.x == 0) trace[7] = global_timer_ns();
     }
+    if (trace && threadIdx.x == 0) trace[11] = global_timer_ns();
     // 1) reduce the WPC warps of each chunk through shared memory as a tree:
     //    at each level warps [h, 2h) add into warps [0, h) (slot-limited
     //    passes); the summation order is fixed, so results are deterministic.
@@ -580,6 +583,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       }
     }
 
+    if (trace && threadIdx.x == 0) trace[8] = global_timer_ns();
     const bool complete = (kb == 0 && ke == p.kk_total);
     if (!complete && kb != 0) {
       // 2a) contributor: this segment ends a tile that another CTA (the one
@@ -606,7 +610,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         if (!aborted && lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
         continue;
       }
-      if (trace && threadIdx.x == 0) trace[6] += 1;
+      if (trace && threadIdx.x == 0) {
+        trace[6] += 1;
+        trace[9] = global_timer_ns();
+      }
       const long long t0 = static_cast<long long>(tile) * units_per_tile;
       const long long c_hi = unit_owner(t0 + units_per_tile - 1, p.units, grid);
       // partials already in shared memory (bulk-copied by the producer)
@@ -652,6 +659,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     }
     // 3) the leader warp of each chunk converts and stores 16-byte rows of C.
     if (threadIdx.x == 0) ++tiles_stored;
+    if (trace && threadIdx.x == 0) trace[10] = global_timer_ns();
     {
       const int n0 = (tile * NC + cc) * 64 + 8 * g;
       float colscale[8];

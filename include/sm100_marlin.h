@@ -223,10 +223,12 @@ int sm100_marlin_set_overlap(int enable);
 
 /* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 the k-th
  * GEMM launch after this call writes into `buf` (device memory, zeroed by the
- * caller, 20 KiB per launch) at offset k * 20 KiB: per CTA 8 uint64 words
+ * caller, 36 KiB per launch) at offset k * 36 KiB: per CTA 16 uint64 words
  * (%globaltimer at kernel entry, first TMA issue, first and last stage
  * consumed, end of the CTA, stage count, fixup count, return from the
- * programmatic-launch wait), then per-stage clock64 stamps of CTA 0.
+ * programmatic-launch wait, then inside the last epilogue: warps reduced,
+ * finisher partials ready, C stores issued, past the dependency wait; words
+ * 12-15 unused), then per-stage clock64 stamps of CTA 0.
  * Returns SM100_MARLIN_ERR_ARGUMENT in normal builds (nothing is recorded).
  * No counterpart in the reference (its profiling is external, via ncu). */
 int sm100_marlin_set_trace_buffer(void* buf);
