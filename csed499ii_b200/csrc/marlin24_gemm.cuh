@@ -154,8 +154,13 @@ struct DecodeCfg {
     return (kSmemBudget - (HEADER + NC * slots * ACC_BYTES + 1023) / 1024 * 1024 -
             (MB == 1 ? 2 * NC * ACC_BYTES : 0) - 1024) / STAGE;
   }
+  // Batch <= 16: one flat pass instead (every warp but the leader writes its
+  // accumulators, the leader adds them in warp order) when the WPC-1 slots
+  // cost the ring no stage.
+  static constexpr bool FLAT_RED = MB == 1 && WPC > 2 && ring_depth(WPC - 1) >= ring_depth(WPC / 2);
   static constexpr int RED_SLOTS =
-      (WPC / 2 > 1 && ring_depth(WPC / 2) + 1 >= ring_depth(1)) ? WPC / 2 : 1;
+      FLAT_RED ? WPC - 1
+               : ((WPC / 2 > 1 && ring_depth(WPC / 2) + 1 >= ring_depth(1)) ? WPC / 2 : 1);
   static constexpr int RED_BYTES = NC * RED_SLOTS * ACC_BYTES;
   // Split-K finisher: room for the partials of up to FIN_SLOTS other CTAs of
   // its tile, bulk-copied in while the finisher still computes (batch <= 16;
@@ -554,12 +559,31 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       if (trace && threadIdx.x == 0) trace[7] = global_timer_ns();
     }
     if (trace && threadIdx.x == 0) trace[11] = global_timer_ns();
-    // 1) reduce the WPC warps of each chunk through shared memory as a tree:
+    // 1) reduce the WPC warps of each chunk through shared memory, flat (see
+    //    FLAT_RED) or as a tree:
     //    at each level warps [h, 2h) add into warps [0, h) (slot-limited
     //    passes); the summation order is fixed, so results are deterministic.
     float4* acc4 = reinterpret_cast<float4*>(&acc[0][0][0][0]);
     const int wk = warp / NC;  // warp index among the warps sharing this chunk
-    for (int h = Cfg::WPC / 2; h >= 1; h /= 2) {
+    if constexpr (Cfg::FLAT_RED) {
+      float4* red4 = reinterpret_cast<float4*>(red) + (cc * Cfg::RED_SLOTS * Cfg::ACC_F4) * 32 + lane;
+      if (wk != 0) {
+#pragma unroll
+        for (int v = 0; v < Cfg::ACC_F4; ++v) red4[((wk - 1) * Cfg::ACC_F4 + v) * 32] = acc4[v];
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+      if (wk == 0) {
+#pragma unroll
+        for (int w = 0; w < Cfg::RED_SLOTS; ++w)
+#pragma unroll
+          for (int v = 0; v < Cfg::ACC_F4; ++v) {
+            const float4 x = red4[(w * Cfg::ACC_F4 + v) * 32];
+            acc4[v].x += x.x; acc4[v].y += x.y; acc4[v].z += x.z; acc4[v].w += x.w;
+          }
+      }
+      named_bar_sync(1, kConsumerWarps * 32);
+    }
+    for (int h = Cfg::FLAT_RED ? 0 : Cfg::WPC / 2; h >= 1; h /= 2) {
       for (int base = 0; base < h; base += Cfg::RED_SLOTS) {
         const int slot_w = wk - h - base;  // writer's slot this pass
         const int slot_r = wk - base;      // reader's slot this pass
