@@ -18,9 +18,15 @@ Lines printed (rank 0, one JSON line):
   inside the timed region.
 * ``roofline`` -- GEMM kernel achieved GB/s vs the measured HBM copy peak.
 * ``cpu_baseline`` -- the CPU oracle (numpy dequantise-then-matmul, the
-  reference's torch fp32 oracle path) on a bounded sample.
+  reference's torch fp32 oracle path) on a bounded sample, plus the variant
+  that decompresses the packed weights on every call.
+* ``detail`` -- per-shape kernel times of the step and a small prefill
+  sample (config 4 shapes, TFLOP/s against the derived 2:4 peak).
 
 ``--impl reference`` times the reference's CPU path (the oracle port) alone.
+``--workload prefill`` runs the config-4 sweep (with the cuSPARSELt bar);
+``--workload ablation`` runs the metadata-cost ablation (the reference's
+``kernel_profile/run.py bench`` protocol).
 """
 from __future__ import annotations
 
@@ -32,6 +38,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -39,8 +47,9 @@ LAYERS = 32
 SHAPES = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]  # (K, N)
 GROUP = 128
 # (batch rows, metadata bits) -> mean DRAM bytes per GEMM launch over SHAPES,
-# from ncu `dram__bytes_read.sum + dram__bytes_write.sum`
-# (profiles/marlin24_decode_llama7b_m16.md).
+# `dram__bytes_read.sum + dram__bytes_write.sum` from one ncu capture of the
+# same kernel and shapes, made separately (ncu cannot run inside this
+# timing); reported as a constant with its source, not measured in the run.
 MEASURED_TRAFFIC = {(16, 4): 20.002e6}
 
 
@@ -312,9 +321,9 @@ def bench_ours(args, torch, dist, rank, world, dev):
         fg.close()
 
     peak, peak_kind = load_peaks()
-    # DRAM bytes (read + write) per launch from one ncu capture of the same
-    # kernel and shapes (profiles/marlin24_decode_llama7b_m16.md), averaged
-    # over the four shapes like `achieved`; only known for the default case.
+    # DRAM bytes (read + write) per launch from a separate ncu capture of the
+    # same kernel and shapes, averaged over the four shapes like `achieved`;
+    # only known for the default case.
     traffic = MEASURED_TRAFFIC.get((M, args.meta_bits))
     achieved = bytes_step / args.layers / len(SHAPES) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
     return dict(
@@ -325,6 +334,9 @@ def bench_ours(args, torch, dist, rank, world, dev):
                  ms_per_step=round(e2e_ms / e2e_steps, 4)),
         roofline=dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s",
                       frac=round(achieved / peak, 4), traffic=traffic,
+                      traffic_source=("constant: ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                      "per launch from a separate capture of this kernel on these "
+                                      "shapes, not measured in this run") if traffic else None,
                       peak_source=f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback"),
     )
 
@@ -332,29 +344,51 @@ def bench_ours(args, torch, dist, rank, world, dev):
 # ----------------------------------------------------------------------------
 # CPU oracle (the reference's dequantise-then-matmul path)
 # ----------------------------------------------------------------------------
-def cpu_reference(M, meta_bits, reps, layers_sample=1, budget_s=25.0):
-    """Time the CPU oracle on one layer's four GEMMs (bounded sample)."""
-    import numpy as np
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
 
+    return platform.processor() or "unknown"
+
+
+def _cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _random_packed(rng, K, N):
+    B = rng.integers(0, 2**32, size=(K // 32, 2 * N), dtype=np.uint64).astype(np.uint32).view(np.int32)
+    nib = rng.choice(np.array([0x4, 0x8, 0x9, 0xC, 0xD, 0xE], dtype=np.uint16), size=(N * K // 16, 4))
+    meta = (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).astype(np.uint16)
+    meta = meta.view(np.int16).reshape(N, K // 16)
+    s = (rng.uniform(0.01, 0.03, size=(K // GROUP, N)) * 2 / 15).astype(np.float16)
+    return B, meta, s
+
+
+def cpu_reference(M, meta_bits, reps, budget_s=25.0):
+    """The reference's CPU path on one Llama-2-7B layer (its four GEMMs):
+    ``A.float() @ W.float()`` with W the oracle's dequantised 2:4 weight,
+    dequantised once (``metadata_decode/smoke.py:26``).  One *step* of this
+    arm is that one layer; ``seconds_per_step`` is its measured median."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import marlin24_oracle as O
 
     rng = np.random.default_rng(0)
     Ws, As = [], {}
     for (K, N) in SHAPES:
-        B = rng.integers(0, 2**32, size=(K // 32, 2 * N), dtype=np.uint64).astype(np.uint32).view(np.int32)
-        nib = rng.choice(np.array([0x4, 0x8, 0x9, 0xC, 0xD, 0xE], dtype=np.uint16), size=(N * K // 16, 4))
-        meta = (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).astype(np.uint16)
-        meta = meta.view(np.int16).reshape(N, K // 16)
-        s = (rng.uniform(0.01, 0.03, size=(K // GROUP, N)) * 2 / 15).astype(np.float16)
+        B, meta, s = _random_packed(rng, K, N)
         Ws.append(O.dequant_2_4(B, meta, s, K, N, GROUP).astype(np.float32))
         As.setdefault(K, rng.standard_normal((M, K)).astype(np.float16).astype(np.float32))
-    try:
-        from threadpoolctl import threadpool_info
-
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count() or 1
     bytes_layer = sum(algo_bytes(M, K, N, meta_bits) for (K, N) in SHAPES)
     times = []
     t_start = time.perf_counter()
@@ -366,10 +400,41 @@ def cpu_reference(M, meta_bits, reps, layers_sample=1, budget_s=25.0):
         if time.perf_counter() - t_start > budget_s:
             break
     t = statistics.median(times)
-    return dict(value=round(bytes_layer / t / 1e9, 3), unit="GB/s", cores=cores, kind="port",
-                sample=(f"one Llama-2-7B layer (4 GEMMs, M={M}) of the 32-layer step; numpy fp32 "
-                        f"A @ dequant(W) with W dequantised once by the oracle; median of {len(times)} reps"),
-                seconds_per_layer=t)
+    return dict(value=round(bytes_layer / t / 1e9, 3), unit="GB/s", cores=_cpu_threads(), kind="port",
+                cpu_model=cpu_model(), os_cpu_count=os.cpu_count(),
+                sample=(f"step = one Llama-2-7B layer (its 4 GEMMs, M={M}) of the 32-layer decode "
+                        f"step; numpy fp32 A @ dequant(W), W dequantised once by the oracle "
+                        f"(the reference's torch fp32 path); median of {len(times)} steps"),
+                seconds_per_step=t, steps_run=len(times))
+
+
+def cpu_reference_decompress(M, reps=3, budget_s=15.0):
+    """The variant that decompresses on every call: the packed (B, meta, s)
+    are expanded to the dense weight (the reference's
+    ``sparse_semi_structured_to_dense_cutlass`` + scale multiply,
+    ``_semi_structured_conversions.py:186-283``, restated by the oracle) and
+    multiplied, per call, on the (4096, 4096) layer."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import marlin24_oracle as O
+
+    K = N = 4096
+    rng = np.random.default_rng(1)
+    B, meta, s = _random_packed(rng, K, N)
+    A = rng.standard_normal((M, K)).astype(np.float16).astype(np.float32)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        W = O.dequant_2_4(B, meta, s, K, N, GROUP).astype(np.float32)
+        _ = A @ W
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    t = statistics.median(times)
+    return dict(value=round(algo_bytes(M, K, N, 4) / t / 1e9, 4), unit="GB/s", cores=_cpu_threads(),
+                kind="port", sample=(f"one (K, N) = (4096, 4096) GEMM at M={M} with the packed weight "
+                                     f"decompressed on every call; median of {len(times)} calls"),
+                us_per_call=round(t * 1e6, 1))
 
 
 PREFILL_SHAPES = [(4096, 4096), (8192, 8192), (4096, 11008)]  # (K, N), BASELINE config 4
@@ -416,6 +481,137 @@ def bench_prefill(args, torch, dev):
             flops_total += fl
             sec_total += t
     return flops_total / sec_total / 1e12, detail
+
+
+def dense_peak():
+    """(dense bf16 TFLOP/s, label): the derived 2:4 peak is twice it."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "derived: 2 x measured dense bf16 (MEASURED_PEAKS.json)"
+    except Exception:
+        return 1590.0, "derived: 2 x fallback dense"
+
+
+PREFILL_SAMPLE = [(2048, 4096, 4096), (8192, 4096, 4096), (2048, 8192, 8192), (8192, 8192, 8192)]
+
+
+def prefill_sample(torch, dev, reps=10):
+    """Config-4 sample carried in the decode line's `detail`: single GEMMs at
+    M = 2048 / 8192 and K = N = 4096 / 8192, inputs resident, CUDA events on
+    the launching stream; TFLOP/s dense-equivalent against the derived 2:4
+    peak."""
+    import csed499ii_b200 as m
+
+    lib = m._ext.load()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4323)
+    stream = torch.cuda.Stream(device=dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dense, kind = dense_peak()
+    out, layers = {}, {}
+    for (M, K, N) in PREFILL_SAMPLE:
+        if (K, N) not in layers:
+            layers[(K, N)] = make_layer(torch, K, N, dev, gen, 4)
+        B, meta, s = layers[(K, N)]
+        ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
+        A = torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
+        C = torch.empty((M, N), dtype=torch.half, device=dev)
+
+        def call():
+            rc = lib.sm100_marlin_mul_2_4(A.data_ptr(), B.data_ptr(), meta.data_ptr(), C.data_ptr(),
+                                          s.data_ptr(), N, M, K, ws.data_ptr(), GROUP // 2, dev.index,
+                                          stream.cuda_stream, -1, -1, -1, 16)
+            if rc != 0:
+                raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                call()
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = ev0.elapsed_time(ev1) * 1e-3 / reps
+        tf = 2.0 * M * N * K / t / 1e12
+        out[f"M{M}_K{K}_N{N}"] = {"us": round(t * 1e6, 1), "TFLOP/s": round(tf, 1),
+                                  "frac_of_2to4_peak": round(tf / (2 * dense), 4)}
+    out["peak"] = {"value": 2 * dense, "unit": "TFLOP/s", "source": kind}
+    return out
+
+
+ABLATION_SHAPES = [(1, 4096, 4096), (16, 4096, 4096), (32, 4096, 4096), (1, 1024, 1024),
+                   (64, 4096, 4096), (2048, 4096, 4096)]
+
+
+def bench_ablation(args, torch, dev, samples=9, graph_calls=100, replays=5):
+    """Metadata-cost ablation, the reference's `kernel_profile/run.py bench`
+    protocol: uniform inputs (random packed codes, scales 0.01, metadata
+    0xEEEE), every variant checked bit-exact against the baseline first, then
+    `graph_calls` calls captured in one CUDA graph per variant, `samples`
+    measurements of `replays` replays each in a shuffled order (seeded), and
+    the median per-call microseconds."""
+    import random
+
+    import csed499ii_b200 as m
+    from csed499ii_b200 import metadata_diagnostics as diag
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(20261019)
+    rows = {}
+    for (M, N, K) in ABLATION_SHAPES:
+        a = torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
+        b = torch.randint(-(2**31), 2**31 - 1, (K // 32, 2 * N), dtype=torch.int32, device=dev,
+                          generator=gen)
+        s = torch.full((K // 128, N), 0.01, dtype=torch.half, device=dev)
+        meta = torch.full((N, K // 16), -4370, dtype=torch.int16, device=dev)
+        c = torch.empty((M, N), dtype=torch.half, device=dev)
+        ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=dev)
+        fns = {"baseline": m.mul_2_4, "no_gmem": diag.no_gmem, "no_reg": diag.no_reg,
+               "no_all": diag.no_all}
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            fns["baseline"](a, b, meta, c, s, ws)
+            torch.cuda.synchronize(dev)
+            ref = c.clone()
+            for name, f in fns.items():
+                c.fill_(float("nan"))
+                f(a, b, meta, c, s, ws)
+                torch.cuda.synchronize(dev)
+                if not torch.equal(c, ref):
+                    raise RuntimeError(f"ablation {name} differs from the baseline at {(M, N, K)}")
+        graphs = {}
+        for name, f in fns.items():
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    f(a, b, meta, c, s, ws)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(graph_calls):
+                    f(a, b, meta, c, s, ws)
+            graphs[name] = g
+        jobs = [(name, i) for name in fns for i in range(samples)]
+        random.Random(20261019).shuffle(jobs)
+        per = {name: [] for name in fns}
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for name, _ in jobs:
+            with torch.cuda.stream(stream):
+                graphs[name].replay()
+                ev0.record(stream)
+                for _ in range(replays):
+                    graphs[name].replay()
+                ev1.record(stream)
+            ev1.synchronize()
+            per[name].append(ev0.elapsed_time(ev1) * 1000 / (graph_calls * replays))
+        med = {name: round(statistics.median(v), 3) for name, v in per.items()}
+        base = med["baseline"]
+        rows[f"M{M}_N{N}_K{K}"] = {"us": med, "saved_vs_baseline": {
+            name: round(1 - med[name] / base, 4) for name in fns if name != "baseline"}}
+        del graphs
+    if m.device_status(dev.index) != 0:
+        raise RuntimeError("a bounded wait timed out during the ablation")
+    return rows
 
 
 def bench_cusparselt(args, torch, dev):
@@ -468,9 +664,12 @@ def main():
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-gather of C fused into the GEMM epilogue (NVLink peer "
                          "stores) or a separate NCCL all-gather")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "ablation"], default="decode",
                     help="decode: Llama-2-7B decode step (config 1, the headline); "
-                         "prefill: compute-bound sweep (config 4)")
+                         "prefill: compute-bound sweep (config 4); ablation: metadata-cost "
+                         "diagnostics (config 4's ablation)")
+    ap.add_argument("--no-prefill-sample", action="store_true",
+                    help="decode: skip the config-4 prefill sample in `detail`")
     ap.add_argument("--no-comparator", action="store_true",
                     help="prefill: skip the cuSPARSELt fp16 2:4 comparator")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -496,11 +695,13 @@ def main():
         if rank != 0:
             return
         ref = cpu_reference(args.m, args.meta_bits, reps=max(args.steps, 1))
+        keys = ("value", "unit", "cores", "kind", "sample", "cpu_model", "os_cpu_count")
         line = dict(metric=metric, value=ref["value"], unit="GB/s", n_gpus=args.gpus,
-                    steps=args.steps, warmup=args.warmup, ms_per_step=round(ref["seconds_per_layer"] * args.layers * 1e3, 3),
+                    steps=ref["steps_run"], warmup=args.warmup,
+                    ms_per_step=round(ref["seconds_per_step"] * 1e3, 3),
                     higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
                     data="synthetic", config=config, impl="reference",
-                    cpu_baseline={k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                    cpu_baseline={k: ref[k] for k in keys},
                     e2e={"value": ref["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                          "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
@@ -524,12 +725,7 @@ def main():
 
     if args.workload == "prefill":
         value, detail = bench_prefill(args, torch, dev)
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                dense = float(json.load(f)["bf16_tflops"])
-            kind = "derived: 2 x measured dense bf16 (MEASURED_PEAKS.json)"
-        except Exception:
-            dense, kind = 1590.0, "derived: 2 x fallback dense"
+        dense, kind = dense_peak()
         line = dict(metric="2:4 W4A16 GEMM dense-equivalent TFLOP/s (prefill sweep, config 4)"
                     + ("" if args.meta_bits == 4 else ", 3-bit metadata"),
                     value=round(value, 1), unit="TFLOP/s", n_gpus=1, steps=args.steps,
@@ -553,11 +749,27 @@ def main():
         if rank == 0:
             print(json.dumps(line), flush=True)
         return
+    if args.workload == "ablation":
+        rows = bench_ablation(args, torch, dev)
+        if rank == 0:
+            print(json.dumps(dict(
+                metric="metadata-cost ablation: per-call us, uniform 0xEEEE metadata (config 4)",
+                unit="us", higher_is_better=False, n_gpus=1, dtype="f16",
+                data="synthetic uniform (random packed INT4 codes, scales 0.01, metadata 0xEEEE)",
+                config={"workload": "kernel_profile/run.py bench protocol: 100 calls per CUDA graph, "
+                                    "9 shuffled samples of 5 replays, median",
+                        "shapes": [f"M{M}_N{N}_K{K}" for (M, N, K) in ABLATION_SHAPES]},
+                detail=rows)), flush=True)
+        return
     res = bench_ours(args, torch, dist, rank, world, dev)
+    if rank == 0 and world == 1 and args.workload == "decode" and not args.no_prefill_sample:
+        res["detail"]["prefill_sample"] = prefill_sample(torch, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ref = cpu_reference(args.m, args.meta_bits, reps=10)
-        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model",
+                                   "os_cpu_count")}
+        cpu["per_call_decompression"] = cpu_reference_decompress(args.m)
     if rank == 0:
         line = dict(metric=metric, value=round(res["value"], 2), unit="GB/s", n_gpus=world,
                     steps=args.steps, warmup=args.warmup, ms_per_step=round(res["ms_step"], 5),

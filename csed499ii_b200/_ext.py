@@ -35,6 +35,8 @@ SIGNATURES = {
     "sm100_marlin_mul_2_4_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp, _c_int, _c_int, _vp, _c_int, _c_int, _c_int,
                                               _c_int]),
+    "sm100_marlin_mul_2_4_meta_diag": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int,
+                                                _vp, _c_int, _c_int, _vp, _c_int]),
     "sm100_marlin_scratch_bytes": (_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "sm100_marlin_meta3_pack": (_c_int, [_vp, _vp, _i64, _vp, _vp]),
     "sm100_marlin_meta3_unpack": (_c_int, [_vp, _vp, _i64, _vp]),

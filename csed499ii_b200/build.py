@@ -1,12 +1,16 @@
 """Build recipe for the in-tree CUDA library (sm_100a only).
 
-``python -m csed499ii_b200.build`` compiles ``csrc/sm100_marlin.cu`` with
-nvcc into ``csed499ii_b200/_lib/libsm100_marlin.so``.  The library is a plain
-C-ABI shared object (no torch, no Python symbols); ``csed499ii_b200._ext``
-loads it with ctypes.
+``python -m csed499ii_b200.build`` compiles every ``csrc/*.cu`` translation
+unit with nvcc (in parallel, objects under ``csed499ii_b200/_build/``) and
+links them into ``csed499ii_b200/_lib/libsm100_marlin.so``: the host launcher
+and C ABI (``sm100_marlin.cu``) and the kernel instances (``k_*.cu``).  The
+library is a plain C-ABI shared object (no torch, no Python symbols);
+``csed499ii_b200._ext`` loads it with ctypes.
 """
 from __future__ import annotations
 
+import concurrent.futures
+import hashlib
 import os
 import shutil
 import subprocess
@@ -28,8 +32,8 @@ NVCC_FLAGS = [
     "--expt-relaxed-constexpr",
     "-Xcompiler",
     "-fPIC,-O3",
-    "-shared",
 ]
+BUILD_DIR = os.path.join(HERE, "_build")
 
 
 def _nvcc() -> str:
@@ -39,10 +43,18 @@ def _nvcc() -> str:
     return cand
 
 
-def _sources():
-    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith((".cu", ".cuh", ".h"))] + [
+def _units():
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith(".cu")]
+
+
+def _headers():
+    return [os.path.join(CSRC, f) for f in sorted(os.listdir(CSRC)) if f.endswith((".cuh", ".h"))] + [
         os.path.join(ROOT, "include", "sm100_marlin.h")
     ]
+
+
+def _sources():
+    return _units() + _headers()
 
 
 def up_to_date() -> bool:
@@ -52,28 +64,59 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in _sources())
 
 
+def _compile(unit: str, obj: str, defines, ptxas_info: bool):
+    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS] + [f"-D{d}" for d in defines]
+    if ptxas_info:
+        cmd += ["-Xptxas", "-v"]
+    cmd += ["-c", "-o", obj + ".tmp", unit]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {os.path.basename(unit)}:\n" + res.stdout + res.stderr)
+    os.replace(obj + ".tmp", obj)
+    return " ".join(cmd), res.stdout + res.stderr
+
+
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False,
           out: str = LIB_PATH, defines=()) -> str:
     """Compile the library if any source is newer than it; return its path.
 
-    ``defines`` (e.g. ``["SM100_MARLIN_TRACE=1"]``) build a variant into
-    ``out``; the default build has none.
+    Each translation unit is recompiled when it or any header is newer than
+    its object.  ``defines`` (e.g. ``["SM100_MARLIN_TRACE=1"]``) build a
+    variant into ``out`` (objects in their own directory); the default build
+    has none.
     """
     if not force and not ptxas_info and not defines and out == LIB_PATH and up_to_date():
         return LIB_PATH
+    tag = hashlib.sha1(" ".join(sorted(defines)).encode()).hexdigest()[:8] if defines else "default"
+    bdir = os.path.join(BUILD_DIR, tag)
+    os.makedirs(bdir, exist_ok=True)
     os.makedirs(os.path.dirname(out), exist_ok=True)
+    newest_header = max(os.path.getmtime(h) for h in _headers())
+    jobs = []
+    objs = []
+    for unit in _units():
+        obj = os.path.join(bdir, os.path.basename(unit)[:-3] + ".o")
+        objs.append(obj)
+        stale = (force or ptxas_info or not os.path.exists(obj)
+                 or os.path.getmtime(obj) < max(os.path.getmtime(unit), newest_header))
+        if stale:
+            jobs.append((unit, obj))
+    workers = max(1, min(len(jobs), os.cpu_count() or 1))
+    with concurrent.futures.ThreadPoolExecutor(max_workers=workers) as pool:
+        futs = [pool.submit(_compile, u, o, defines, ptxas_info) for u, o in jobs]
+        for f in futs:
+            cmd, log = f.result()
+            if verbose:
+                print(cmd, flush=True)
+            if verbose or ptxas_info:
+                sys.stdout.write(log)
     tmp = out + ".tmp"
-    cmd = [_nvcc(), *ARCH_FLAGS, *NVCC_FLAGS] + [f"-D{d}" for d in defines]
-    if ptxas_info:
-        cmd += ["-Xptxas", "-v"]
-    cmd += ["-cudart", "static", "-o", tmp, os.path.join(CSRC, "sm100_marlin.cu")]
+    cmd = [_nvcc(), *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
-    if verbose or ptxas_info:
-        sys.stdout.write(res.stdout + res.stderr)
+        raise RuntimeError("linking the library failed:\n" + res.stdout + res.stderr)
     os.replace(tmp, out)
     return out
 

@@ -24,6 +24,19 @@ enum : int {
   kStatusGatherWaitTimeout = 8,  // fused all-gather waited too long for other ranks' blocks
 };
 
+// Metadata-cost diagnostics (a kernel template parameter DIAG, a bit set; 0
+// in every production instance).  They measure what the metadata path costs,
+// as the reference's constant-metadata ablations do
+// (kernel_experiments/sparse_marlin/kernel_profile/setup.py:14-38), and are
+// only correct for inputs whose metadata is the uniform pattern 0xEEEE:
+//   kDiagNoGmem  the metadata is not copied from global memory; every stage's
+//                metadata region holds 0xEEEE from kernel start and is read
+//                from shared memory as usual;
+//   kDiagNoReg   the metadata is copied as usual, but the kernel takes a
+//                constant register instead of loading it from shared memory.
+enum : int { kDiagNoGmem = 1, kDiagNoReg = 2 };
+constexpr uint32_t kDiagMetaWord = 0xEEEEEEEEu;
+
 // Upper bound for any single wait, in nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 500ull * 1000ull * 1000ull;
 
@@ -108,7 +121,7 @@ enum : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGeluTanh = 3 };
 
 // Out of line: inlined, the activations' math grew the decode kernel enough
 // to cost it 7 % even with the epilogue off (2048 vs 1904 GB/s, same box).
-__device__ __noinline__ float epilogue_act_call(float x, int act) {
+static __device__ __noinline__ float epilogue_act_call(float x, int act) {
   if (act == kActRelu) return fmaxf(x, 0.f);
   if (act == kActSilu) return x / (1.f + __expf(-x));
   if (act == kActGeluTanh) {

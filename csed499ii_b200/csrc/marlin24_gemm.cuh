@@ -205,9 +205,10 @@ __device__ __forceinline__ void fence_acq_rel_gpu() {
 // EPI: the fused bias / activation epilogue is compiled in (a separate
 // instantiation: even out of line, the epilogue code cost the plain kernel
 // 3.5 %, 2059 vs 1988 GB/s on the same box).
-template <int NC, int MB, int NH_LAST, bool META3, bool GROUPED, bool EPI>
+template <int NC, int MB, int NH_LAST, bool META3, bool GROUPED, bool EPI, int DIAG = 0>
 __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     marlin24_decode_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(DIAG == 0 || (!META3 && !EPI), "diagnostics: 4-bit metadata, plain store");
   using Cfg = DecodeCfg<NC, MB, META3>;
   constexpr int SK = Cfg::SK;
   constexpr int D = Cfg::DEPTH;
@@ -247,6 +248,13 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     mbar_init(smem_addr(fin_bar), 1);
     fence_mbar_init();
   }
+  if constexpr ((DIAG & kDiagNoGmem) != 0) {
+    // uniform metadata in every stage's region, written once (never copied)
+    for (int st = 0; st < D; ++st) {
+      uint32_t* mreg = reinterpret_cast<uint32_t*>(smem + Cfg::RING_OFF + st * Cfg::STAGE + Cfg::OFF_M);
+      for (int i = threadIdx.x; i < SK * Cfg::M_ROW / 4; i += blockDim.x) mreg[i] = kDiagMetaWord;
+    }
+  }
   // Let the next kernel on the stream start its prologue and weight prefetch
   // while this one runs (it waits for this grid before touching anything
   // this kernel reads or writes besides the weights).
@@ -274,7 +282,8 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     if (lane == 0) {
       const uint64_t pol_stream = policy_evict_first();
       const uint64_t pol_keep = policy_evict_last();
-      const uint32_t tx = GROUPED ? Cfg::STAGE_TX_SCALE : Cfg::STAGE_TX_NOSCALE;
+      const uint32_t tx = (GROUPED ? Cfg::STAGE_TX_SCALE : Cfg::STAGE_TX_NOSCALE) -
+                          ((DIAG & kDiagNoGmem) ? SK * Cfg::M_ROW : 0);
       // With programmatic dependent launch the previous kernel on the stream
       // may still be running: the weight parts of the first ring's worth of
       // stages are issued before griddepcontrol.wait; the activation parts,
@@ -324,8 +333,9 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
           const uint32_t st = ring_base + slot * Cfg::STAGE;
           mbar_arrive_expect_tx(full, tx);
           tma_load_2d(st + Cfg::OFF_B, &p.tm_b, tile * 64 * NC, kk0, full, pol_stream);
-          tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, tile * (Cfg::M_BLK / 8) * NC, kk0, full,
-                      pol_stream);
+          if constexpr ((DIAG & kDiagNoGmem) == 0)
+            tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, tile * (Cfg::M_BLK / 8) * NC, kk0, full,
+                        pol_stream);
           if (GROUPED)
             tma_load_2d(st + Cfg::OFF_S, &p.tm_s, tile * 16 * NC, kk0 >> 2, full, pol_keep);
           if (waited) {
@@ -462,6 +472,9 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
               const uint32_t a = lds32(st + m_off + r * Cfg::M_ROW);
               const uint32_t b = lds32(st + m_off + r * Cfg::M_ROW + 64);
               meta3_pair_decode(a, b, (lane & 16) != 0, mw[0], mw[1]);
+            } else if constexpr ((DIAG & kDiagNoReg) != 0) {
+              mw[0] = kDiagMetaWord;
+              mw[1] = kDiagMetaWord;
             } else {
               ldmatrix_x2(mw, st + m_off + r * Cfg::M_ROW);
             }
@@ -762,7 +775,6 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         const unsigned long long* own = p.gather_flag[p.gather_rank];
         unsigned long long t0 = 0;
         uint32_t polls = 0;
-        bool ok = true;
         while (ld_acquire_sys_u64(own) < target) {
           if ((++polls & 63u) != 0) continue;
           const unsigned long long now = global_timer_ns();
@@ -770,11 +782,14 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
             t0 = now;
           } else if (now - t0 > kWaitLimitNs) {
             atomicOr(p.status, kStatusGatherWaitTimeout);
-            ok = false;
             break;
           }
         }
-        if (ok) *p.gather_seen = target;
+        // Advanced on expiry too: arrivals that come late still count toward
+        // this call's target, so the next call on the buffer waits for its own
+        // blocks rather than for this call's stragglers.  The status bit tells
+        // the host that this call's output is incomplete.
+        *p.gather_seen = target;
       }
     }
   }

@@ -495,10 +495,13 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
 // per 32-K row and 64-feature chunk 48 words instead of 64; each dequantising
 // thread decodes its one 4-bit word from two of them before the copy into
 // tensor memory, so the MMAs are unchanged.
-template <int NG, bool GROUPED, bool EPI, bool META3 = false>
+// DIAG: metadata-cost diagnostics (kDiagNoGmem / kDiagNoReg of
+// device_primitives.cuh; 0 in production instances).
+template <int NG, bool GROUPED, bool EPI, bool META3 = false, int DIAG = 0>
 __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     marlin24_prefill_sp2_kernel(const __grid_constant__ PrefillParams p) {
   using Cfg = PrefillSp2Cfg<NG>;
+  static_assert(DIAG == 0 || (!META3 && !EPI), "diagnostics: 4-bit metadata, plain store");
   constexpr int D = Cfg::DEPTH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -529,6 +532,13 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     *abort_flag = 0;
   }
   if (threadIdx.x < D || threadIdx.x == 32) fence_mbar_init();
+  if constexpr ((DIAG & kDiagNoGmem) != 0) {
+    // uniform metadata in every stage's region, written once (never copied)
+    for (int st = 0; st < D; ++st) {
+      uint32_t* mreg = reinterpret_cast<uint32_t*>(smem + Cfg::HEADER + st * Cfg::STAGE + Cfg::OFF_M);
+      for (int i = threadIdx.x; i < 2048 / 4; i += blockDim.x) mreg[i] = kDiagMetaWord;
+    }
+  }
   if (warp == 1) tmem_alloc_pair(smem_addr(tmem_slot), Cfg::TMEM_COLS);
   if (threadIdx.x == 0) {
     prefetch_tmap(&p.tm_act);
@@ -559,7 +569,7 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
     // packed codes 4 x 1 KB, metadata 4 x 512 B (4-bit) or 4 x 384 B (3-bit)
-    const uint32_t txw = 4096 + (META3 ? 1536 : 2048) + (GROUPED ? 256 : 0);
+    const uint32_t txw = 4096 + ((DIAG & kDiagNoGmem) ? 0 : (META3 ? 1536 : 2048)) + (GROUPED ? 256 : 0);
     const int act_row = m_tile * 256 + static_cast<int>(rank) * Cfg::ROWS;
     for (int ks = 0; ks < ksteps; ++ks) {
       const int slot = ks % D;
@@ -574,8 +584,9 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
         const uint32_t wfull = smem_addr(&wfull_bar[slot]);
         mbar_arrive_expect_tx(wfull, txw);
         tma_load_2d(st + Cfg::OFF_B, &p.tm_b, n_tile * 128, ks * 4, wfull, pol_stream);
-        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * (META3 ? 48 : 64), ks * 4, wfull,
-                    pol_stream);
+        if constexpr ((DIAG & kDiagNoGmem) == 0)
+          tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, n_tile * (META3 ? 48 : 64), ks * 4, wfull,
+                      pol_stream);
         if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, n_tile * 32, ks, wfull, pol_keep);
         // both CTAs' activation halves count on the even CTA's ready barrier
         const uint32_t ready = smem_addr(&aready_bar[slot]);
@@ -669,6 +680,8 @@ __global__ void __launch_bounds__(PrefillSp2Cfg<NG>::THREADS, 1)
             mw = decode24_low(m3_upper ? (b >> 8) : __funnelshift_r(a, b, 24));
           else
             mw = decode24_high(m3_upper ? __funnelshift_r(a, b, 16) : a);
+        } else if constexpr ((DIAG & kDiagNoReg) != 0) {
+          mw = kDiagMetaWord;
         } else {
           mw = lds32(st + Cfg::OFF_M + kk * 512 + m_word);
         }

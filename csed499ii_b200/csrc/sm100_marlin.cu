@@ -20,13 +20,7 @@
 #include <utility>
 
 #include "../../include/sm100_marlin.h"
-#include "device_primitives.cuh"
-#include "marlin24_gemm.cuh"
-#include "marlin24_prefill.cuh"
-#include "marlin24_prefill_persistent.cuh"
-#include "marlin24_prefill_sparse.cuh"
-#include "packer.cuh"
-#include "meta3_codec.cuh"
+#include "launch.cuh"
 
 namespace sm100 {
 
@@ -41,8 +35,15 @@ constexpr size_t kNoAllocScratchBytes = 8u << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-
 thread_local std::string t_last_cuda_error;
+}  // namespace
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = cudaGetErrorString(e);
+  return SM100_MARLIN_ERR_CUDA;
+}
+
+namespace {
 
 // Programmatic dependent launch between consecutive GEMM launches (on by
 // default; SM100_MARLIN_PDL=0 or sm100_marlin_set_overlap(0) turns it off).
@@ -56,14 +57,27 @@ bool pdl_enabled() {
   return env_on;
 }
 
+// Tuning knobs.  Builds with -DSM100_MARLIN_TUNING=1 (experiments only) read
+// them from the environment once per process; the default build compiles
+// them out and uses the measured defaults given at each call site.  The one
+// supported environment switch is SM100_MARLIN_PDL (above).
+#ifndef SM100_MARLIN_TUNING
+#define SM100_MARLIN_TUNING 0
+#endif
+int tuning_knob(const char* name, int dflt) {
+#if SM100_MARLIN_TUNING
+  const char* e = std::getenv(name);
+  return e ? std::atoi(e) : dflt;
+#else
+  (void)name;
+  return dflt;
+#endif
+}
+
 // Stages whose weights a kernel may stream before the previous kernel on the
-// stream has completed (default: the whole ring).  SM100_MARLIN_PREFETCH=n
-// caps it (tuning knob).
+// stream has completed (default: the whole ring; knob SM100_MARLIN_PREFETCH).
 int prefetch_stages() {
-  static const int v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFETCH");
-    return e ? std::atoi(e) : (1 << 30);
-  }();
+  static const int v = tuning_knob("SM100_MARLIN_PREFETCH", 1 << 30);
   return v;
 }
 
@@ -72,10 +86,6 @@ unsigned long long* g_trace_buffer = nullptr;
 // Trace builds: launch k writes its records at g_trace_buffer + k * kTraceLaunchWords.
 long long g_trace_launch = 0;
 
-int cuda_fail(cudaError_t e) {
-  t_last_cuda_error = cudaGetErrorString(e);
-  return SM100_MARLIN_ERR_CUDA;
-}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -138,7 +148,9 @@ int get_scratch(int dev, cudaStream_t stream, size_t need, void** out) {
 
 // Device address of g_noalloc_scratch on `dev` (the host-side symbol is only
 // a stand-in, never a device pointer).  Resolved once per device, with that
-// device current; the first noalloc call on a device does it.
+// device current; the first noalloc call on a device does it.  The cached
+// address is valid as long as the device's primary context lives: after a
+// cudaDeviceReset it would point at freed memory (documented in the header).
 int noalloc_scratch(int dev, void** out) {
   static std::mutex mu;
   static void* ptr[64] = {};
@@ -196,12 +208,9 @@ int device_status_ptr(int dev, int** out) {
 // that completes the tile, which puts the split-K hand-over on the critical
 // path.  So: the widest tile that still gives every CTA at least one tile
 // boundary, else one chunk (measured best for every Llama-2-7B shape).
-// SM100_MARLIN_NC=1|2|4 overrides (tuning knob).
+// Knob SM100_MARLIN_NC=1|2|4 forces a width.
 int choose_nc(int n_out, int sms) {
-  static const int forced = [] {
-    const char* e = std::getenv("SM100_MARLIN_NC");
-    return e ? std::atoi(e) : 0;
-  }();
+  static const int forced = tuning_knob("SM100_MARLIN_NC", 0);
   const int chunks = n_out / 64;
   if ((forced == 1 || forced == 2 || forced == 4) && chunks % forced == 0) return forced;
   for (int nc : {4, 2})
@@ -240,8 +249,12 @@ Plan make_plan(int n_out, int m_rows, int k_in, int sms) {
   // Measured at M = 16: K = N = 4096 5.87 vs 7.24 us; deeper tiles stream too
   // slowly on fewer SMs (K = 11008, N = 4096: 11.0 vs 10.0 us).
   if (n_tiles <= sms && kk <= 4 * pl.sk) pl.grid = static_cast<int>(n_tiles);
-  // one fp32 partial tile (nc chunks x 16*mb rows x 64 columns) per CTA
-  pl.scratch = static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 4096;
+  // Split-K happens when some CTA's unit range starts inside a tile: never
+  // with one unit per tile or when the CTAs divide the tiles evenly.  Then
+  // one fp32 partial tile (nc chunks x 16*mb rows x 64 columns) per CTA.
+  const long long upt = kk / pl.unit_kk;
+  const bool split = upt > 1 && n_tiles % pl.grid != 0;
+  pl.scratch = split ? static_cast<size_t>(pl.grid) * pl.nc * pl.mb * 4096 : 0;
   return pl;
 }
 
@@ -387,37 +400,11 @@ int encode_maps(GemmParams& p, const Plan& pl, const void* A, const void* B, con
   return SM100_MARLIN_OK;
 }
 
-template <int NC, int MB, int NH, bool META3, bool GROUPED, bool EPI>
-int launch_one(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
-  using Cfg = DecodeCfg<NC, MB, META3>;
-  static bool attr_set[64] = {};
-  auto kern = marlin24_decode_kernel<NC, MB, NH, META3, GROUPED, EPI>;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(Cfg::THREADS);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) return cuda_fail(e);
-  e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
-}
-
-template <bool META3, bool GROUPED, bool EPI>
+template <bool META3, bool GROUPED, bool EPI, int DIAG = 0>
 int dispatch_g(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
 #define SM100_CASE(NC_, MB_, NH_)                                            \
   if (pl.nc == NC_ && pl.mb == MB_ && pl.nh_last == NH_)                     \
-    return launch_one<NC_, MB_, NH_, META3, GROUPED, EPI>(p, pl.grid, dev, stream);
+    return launch_decode<NC_, MB_, NH_, META3, GROUPED, EPI, DIAG>(p, pl.grid, dev, stream);
 #define SM100_CASES_NC(NC_) \
   SM100_CASE(NC_, 1, 1)     \
   SM100_CASE(NC_, 1, 2)     \
@@ -432,7 +419,16 @@ int dispatch_g(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream
 }
 
 template <bool META3>
-int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream) {
+int dispatch(const GemmParams& p, const Plan& pl, int dev, cudaStream_t stream, int diag) {
+  if (!META3 && diag != 0) {
+    // metadata diagnostics: grouped scales, plain store only
+    if (!p.grouped || p.bias != nullptr || p.act != kActNone) return SM100_MARLIN_ERR_ARGUMENT;
+    if (diag == kDiagNoGmem) return dispatch_g<false, true, false, kDiagNoGmem>(p, pl, dev, stream);
+    if (diag == kDiagNoReg) return dispatch_g<false, true, false, kDiagNoReg>(p, pl, dev, stream);
+    if (diag == (kDiagNoGmem | kDiagNoReg))
+      return dispatch_g<false, true, false, kDiagNoGmem | kDiagNoReg>(p, pl, dev, stream);
+    return SM100_MARLIN_ERR_ARGUMENT;
+  }
   if (p.bias != nullptr || p.act != kActNone)
     return p.grouped ? dispatch_g<META3, true, true>(p, pl, dev, stream)
                      : dispatch_g<META3, false, true>(p, pl, dev, stream);
@@ -466,172 +462,62 @@ int check_reference_shape(int prob_m, int prob_n, int prob_k, int groupsize, int
 }
 
 // Batches above this many rows go to the tensor-memory (tcgen05) kernel in
-// one launch instead of 64-row decode launches.  SM100_MARLIN_PREFILL_MIN=n
-// changes it (tuning knob; a very large value disables the prefill kernel).
+// one launch instead of 64-row decode launches (knob SM100_MARLIN_PREFILL_MIN;
+// a very large value disables the prefill kernel).
 int prefill_min_rows() {
-  static const int v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_MIN");
-    return e ? std::atoi(e) : 64;
-  }();
+  static const int v = tuning_knob("SM100_MARLIN_PREFILL_MIN", 64);
   return v;
 }
 
-// Groups of dequantising warps per prefill CTA (SM100_MARLIN_PREFILL_GROUPS=1|2|4,
-// tuning knob).  Default 4: measured 928 / 1003 / 1041 TFLOP/s for 1 / 2 / 4
+// Groups of dequantising warps per prefill CTA (knob SM100_MARLIN_PREFILL_GROUPS
+// = 1|2|4).  Default 4: measured 928 / 1003 / 1041 TFLOP/s for 1 / 2 / 4
 // groups over the prefill sweep.
 int prefill_groups() {
   static const int v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_GROUPS");
-    const int g = e ? std::atoi(e) : 4;
+    const int g = tuning_knob("SM100_MARLIN_PREFILL_GROUPS", 4);
     return (g == 1 || g == 2) ? g : 4;
   }();
   return v;
 }
 
-// Groups of dequantising warps for the sparse prefill kernel
-// (SM100_MARLIN_PREFILL_SPARSE_GROUPS=1|2|4, tuning knob).  Default 4:
-// 1199 / 1246 / 1294 TFLOP/s for 1 / 2 / 4 groups over the prefill sweep.
+// Groups of dequantising warps for the sparse prefill kernel (knob
+// SM100_MARLIN_PREFILL_SPARSE_GROUPS = 1|2|4).  Default 4: 1199 / 1246 / 1294
+// TFLOP/s for 1 / 2 / 4 groups over the prefill sweep.
 int prefill_groups_sparse() {
   static const int v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_SPARSE_GROUPS");
-    const int g = e ? std::atoi(e) : 4;
+    const int g = tuning_knob("SM100_MARLIN_PREFILL_SPARSE_GROUPS", 4);
     return (g == 1 || g == 2) ? g : 4;
   }();
   return v;
 }
 
-template <int BN, int NG, bool GROUPED>
-int launch_prefill_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
-  using Cfg = PrefillCfg<BN, NG>;
-  static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_kernel<BN, NG, GROUPED>;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
-  const dim3 grid(p.N / 128, (p.M + BN - 1) / BN);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
-}
-
-// Structured-sparse prefill kernel (tcgen05.mma.sp) for K % 128 == 0
-// (SM100_MARLIN_PREFILL_SPARSE=0 selects the dense-expansion kernel; tuning
-// knob).  SM100_MARLIN_PREFILL_BN=128|256 forces its batch tile.
+// Structured-sparse prefill kernel (tcgen05.mma.sp) for K % 128 == 0 (knob
+// SM100_MARLIN_PREFILL_SPARSE=0 selects the dense-expansion kernel; knob
+// SM100_MARLIN_PREFILL_BN=128|256 forces its batch tile).
 bool prefill_sparse_enabled() {
-  static const bool v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_SPARSE");
-    return !(e && e[0] == '0');
-  }();
+  static const bool v = tuning_knob("SM100_MARLIN_PREFILL_SPARSE", 1) != 0;
   return v;
 }
 
 int prefill_forced_bn() {
   static const int v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_BN");
-    const int b = e ? std::atoi(e) : 0;
+    const int b = tuning_knob("SM100_MARLIN_PREFILL_BN", 0);
     return (b == 128 || b == 256) ? b : 0;
   }();
   return v;
 }
 
-template <int BN, int NG, bool GROUPED>
-int launch_prefill_sp_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
-  using Cfg = PrefillSpCfg<BN, NG>;
-  static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_sp_kernel<BN, NG, GROUPED>;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
-  const dim3 grid(p.N / 128, (p.M + BN - 1) / BN);
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
-}
-
-// CTA-pair form: 2-CTA clusters along the features, grid (N/128, M/256).
-template <int NG, bool GROUPED, bool EPI, bool META3 = false>
-int launch_prefill_sp2_cfg(const PrefillParams& p, int dev, cudaStream_t stream) {
-  using Cfg = PrefillSp2Cfg<NG>;
-  static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_sp2_kernel<NG, GROUPED, EPI, META3>;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.N / 128, (p.M + 255) / 256);
-  cfg.blockDim = dim3(Cfg::THREADS);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
-}
-
-// Persistent form: one 2-CTA cluster per SM pair, looping over tiles.
-template <int NG, bool GROUPED, bool EPI>
-int launch_prefill_sp2p_cfg(const PrefillParams& p, int dev, int sms, cudaStream_t stream) {
-  using Cfg = PrefillSp2pCfg<NG>;
-  static bool attr_set[64] = {};
-  auto kern = marlin24_prefill_sp2p_kernel<NG, GROUPED, EPI>;
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
-  }
-  const int tiles = (p.N / 256) * ((p.M + 255) / 256);
-  const int max_clusters = sms / 2 > 0 ? sms / 2 : 1;
-  const int clusters = tiles < max_clusters ? tiles : max_clusters;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(Cfg::THREADS);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
-}
-
-// SM100_MARLIN_PREFILL_PERSISTENT=1 runs the CTA-pair prefill persistently
-// (tuning / comparison knob).
-bool prefill_persistent_enabled() {
-  static const bool v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_PERSISTENT");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
-
-// SM100_MARLIN_PREFILL_PAIR=0 keeps 256-row prefill tiles on one CTA
-// (tuning / comparison knob; default: CTA pairs).
+// Knob SM100_MARLIN_PREFILL_PAIR=0 keeps 256-row prefill tiles on one CTA
+// (default: CTA pairs whenever N % 256 == 0).
 bool prefill_pair_enabled() {
-  static const bool v = [] {
-    const char* e = std::getenv("SM100_MARLIN_PREFILL_PAIR");
-    return !(e && e[0] == '0');
-  }();
+  static const bool v = tuning_knob("SM100_MARLIN_PREFILL_PAIR", 1) != 0;
   return v;
 }
 
 // The structured-sparse form: K steps of 64 (as the dense form).
 int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const void* meta,
-                       const void* s, int dev, int sms, cudaStream_t stream, int meta_bits) {
+                       const void* s, int dev, int sms, cudaStream_t stream, int meta_bits,
+                       int diag) {
   const uint64_t N = p.N, K = p.K;
   const int n_tiles = p.N / 128;
   // CTA pairs (256 features x 256 rows, 128-K steps) whenever the pair's 256
@@ -641,8 +527,9 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   // quarter of the SMs idle (the 128-row tile is ~2x slower per CTA).
   int bn = prefill_forced_bn();
   const bool pair = p.N % 256 == 0 && prefill_pair_enabled() && bn != 128;
-  // 3-bit metadata: CTA-pair kernel only (the caller routes nothing else here)
-  if (meta_bits == 3 && !pair) return SM100_MARLIN_ERR_KERN_SHAPE;
+  // 3-bit metadata and the metadata diagnostics: CTA-pair kernel only (the
+  // caller routes nothing else here)
+  if ((meta_bits == 3 || diag != 0) && (!pair || p.K % 128 != 0)) return SM100_MARLIN_ERR_KERN_SHAPE;
   if (bn == 0)
     bn = pair || (p.M > 128 && 4ll * n_tiles * ((p.M + 255) / 256) >= 3ll * sms) ? 256 : 128;
   int rc;
@@ -685,22 +572,25 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
                    2 * N, 128, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const bool epi = p.bias != nullptr || p.act != kActNone;
+    if (diag != 0) {
+      if (!p.grouped || epi || meta_bits != 4) return SM100_MARLIN_ERR_ARGUMENT;
+      if (diag == kDiagNoGmem) return launch_prefill_sp2<4, true, false, false, kDiagNoGmem>(p, dev, stream);
+      if (diag == kDiagNoReg) return launch_prefill_sp2<4, true, false, false, kDiagNoReg>(p, dev, stream);
+      if (diag == (kDiagNoGmem | kDiagNoReg))
+        return launch_prefill_sp2<4, true, false, false, kDiagNoGmem | kDiagNoReg>(p, dev, stream);
+      return SM100_MARLIN_ERR_ARGUMENT;
+    }
     if (meta_bits == 3)
-      return p.grouped ? (epi ? launch_prefill_sp2_cfg<4, true, true, true>(p, dev, stream)
-                              : launch_prefill_sp2_cfg<4, true, false, true>(p, dev, stream))
-                       : (epi ? launch_prefill_sp2_cfg<4, false, true, true>(p, dev, stream)
-                              : launch_prefill_sp2_cfg<4, false, false, true>(p, dev, stream));
-    if (prefill_persistent_enabled() && ng == 4)
-      return p.grouped ? (epi ? launch_prefill_sp2p_cfg<4, true, true>(p, dev, sms, stream)
-                              : launch_prefill_sp2p_cfg<4, true, false>(p, dev, sms, stream))
-                       : (epi ? launch_prefill_sp2p_cfg<4, false, true>(p, dev, sms, stream)
-                              : launch_prefill_sp2p_cfg<4, false, false>(p, dev, sms, stream));
-#define SM100_PREFILL_SP2(NG_)                                                       \
-  if (ng == NG_)                                                                     \
-    return p.grouped ? (epi ? launch_prefill_sp2_cfg<NG_, true, true>(p, dev, stream)   \
-                            : launch_prefill_sp2_cfg<NG_, true, false>(p, dev, stream)) \
-                     : (epi ? launch_prefill_sp2_cfg<NG_, false, true>(p, dev, stream)  \
-                            : launch_prefill_sp2_cfg<NG_, false, false>(p, dev, stream));
+      return p.grouped ? (epi ? launch_prefill_sp2<4, true, true, true, 0>(p, dev, stream)
+                              : launch_prefill_sp2<4, true, false, true, 0>(p, dev, stream))
+                       : (epi ? launch_prefill_sp2<4, false, true, true, 0>(p, dev, stream)
+                              : launch_prefill_sp2<4, false, false, true, 0>(p, dev, stream));
+#define SM100_PREFILL_SP2(NG_)                                                            \
+  if (ng == NG_)                                                                          \
+    return p.grouped ? (epi ? launch_prefill_sp2<NG_, true, true, false, 0>(p, dev, stream)   \
+                            : launch_prefill_sp2<NG_, true, false, false, 0>(p, dev, stream)) \
+                     : (epi ? launch_prefill_sp2<NG_, false, true, false, 0>(p, dev, stream)  \
+                            : launch_prefill_sp2<NG_, false, false, false, 0>(p, dev, stream));
     SM100_PREFILL_SP2(1)
     SM100_PREFILL_SP2(2)
     SM100_PREFILL_SP2(4)
@@ -709,8 +599,8 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   }
 #define SM100_PREFILL_SP(BN_, NG_)                                                   \
   if (bn == BN_ && ng == NG_)                                                        \
-    return p.grouped ? launch_prefill_sp_cfg<BN_, NG_, true>(p, dev, stream)        \
-                     : launch_prefill_sp_cfg<BN_, NG_, false>(p, dev, stream);
+    return p.grouped ? launch_prefill_sp<BN_, NG_, true>(p, dev, stream)        \
+                     : launch_prefill_sp<BN_, NG_, false>(p, dev, stream);
   SM100_PREFILL_SP(128, 1)
   SM100_PREFILL_SP(128, 2)
   SM100_PREFILL_SP(128, 4)
@@ -725,7 +615,7 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
 // metadata): one 128 x BN output tile per CTA on the tcgen05 kernels.
 int mul_prefill(const void* A, const void* B, const void* meta, void* C, const void* s, int n_out,
                 int m_rows, int k_in, int groupsize, int dev, int sms, cudaStream_t stream,
-                int* status, const void* bias, int act, int meta_bits) {
+                int* status, const void* bias, int act, int meta_bits, int diag) {
   PrefillParams p;
   p.s = static_cast<const uint8_t*>(s);
   p.C = static_cast<half*>(C);
@@ -736,8 +626,8 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   p.N = n_out;
   p.K = k_in;
   p.grouped = groupsize != -1 ? 1 : 0;
-  if (meta_bits == 3 || (prefill_sparse_enabled() && k_in % 128 == 0))
-    return mul_prefill_sparse(p, A, B, meta, s, dev, sms, stream, meta_bits);
+  if (meta_bits == 3 || diag != 0 || (prefill_sparse_enabled() && k_in % 128 == 0))
+    return mul_prefill_sparse(p, A, B, meta, s, dev, sms, stream, meta_bits, diag);
   const int n_tiles = n_out / 128;
   const int bn = (m_rows >= 256 && static_cast<long long>(n_tiles) * ((m_rows + 255) / 256) >= sms)
                      ? 256 : 128;
@@ -760,8 +650,8 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   }
 #define SM100_PREFILL(BN_, NG_)                                                      \
   if (bn == BN_ && prefill_groups() == NG_)                                         \
-    return p.grouped ? launch_prefill_cfg<BN_, NG_, true>(p, dev, stream)           \
-                     : launch_prefill_cfg<BN_, NG_, false>(p, dev, stream);
+    return p.grouped ? launch_prefill_dense<BN_, NG_, true>(p, dev, stream)           \
+                     : launch_prefill_dense<BN_, NG_, false>(p, dev, stream);
   SM100_PREFILL(256, 2)
   SM100_PREFILL(256, 1)
   SM100_PREFILL(256, 4)
@@ -784,7 +674,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
              int prob_n, int prob_k, void* workspace, int groupsize, int dev, void* stream_v,
              int thread_k, int thread_m, int sms, int max_par, int meta_bits, void* scratch,
              size_t scratch_bytes, const GatherArgs* gather = nullptr, const void* bias = nullptr,
-             int act = 0) {
+             int act = 0, int diag = 0) {
   (void)max_par;
   if (act < 0 || act > 3) return SM100_MARLIN_ERR_ARGUMENT;
   if (bias != nullptr && !aligned16(bias)) return SM100_MARLIN_ERR_ALIGNMENT;
@@ -827,7 +717,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     rc = device_status_ptr(dev, &status);
     if (rc != SM100_MARLIN_OK) return rc;
     return mul_prefill(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
-                       status, bias, act, meta_bits);
+                       status, bias, act, meta_bits, diag);
   }
 
   const int chunk_rows = prob_n < 64 ? prob_n : 64;
@@ -887,7 +777,8 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     }
     rc = encode_maps(p, pl, a_rows, B, meta, s, meta_bits);
     if (rc != SM100_MARLIN_OK) return rc;
-    rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream) : dispatch<false>(p, pl, dev, stream);
+    rc = meta_bits == 3 ? dispatch<true>(p, pl, dev, stream, 0)
+                        : dispatch<false>(p, pl, dev, stream, diag);
     if (rc != SM100_MARLIN_OK) return rc;
   }
   return SM100_MARLIN_OK;
@@ -957,6 +848,16 @@ int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta,
   return rc;
 }
 
+int sm100_marlin_mul_2_4_meta_diag(const void* A, const void* B, const void* meta, void* C,
+                                   const void* s, int prob_m, int prob_n, int prob_k,
+                                   void* workspace, int groupsize, int dev, void* stream,
+                                   int variant) {
+  if (variant < 1 || variant > 3) return SM100_MARLIN_ERR_ARGUMENT;
+  if (groupsize == -1) return SM100_MARLIN_ERR_ARGUMENT;
+  return mul_impl(A, B, meta, C, s, prob_m, prob_n, prob_k, workspace, groupsize, dev, stream, -1,
+                  -1, -1, 16, 4, nullptr, 0, nullptr, nullptr, 0, variant);
+}
+
 size_t sm100_marlin_scratch_bytes(int prob_m, int prob_n, int prob_k, int dev, int sms) {
   if (prob_m <= 0 || prob_n <= 0 || prob_k <= 0) return 0;
   if (sms == -1 && device_sms(dev, &sms) != SM100_MARLIN_OK) return 0;
@@ -973,15 +874,7 @@ int sm100_marlin_meta3_pack(const void* meta, void* out, int64_t n_int16, void* 
   if ((reinterpret_cast<uintptr_t>(meta) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u) ||
       (reinterpret_cast<uintptr_t>(err_count) & 3u))
     return SM100_MARLIN_ERR_ALIGNMENT;
-  const int64_t pairs = n_int16 / 8;
-  const int threads = 256;
-  const int64_t blocks = (pairs + threads - 1) / threads;
-  meta3_pack_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                      reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint32_t*>(meta), static_cast<uint32_t*>(out), pairs,
-      static_cast<uint32_t*>(err_count));
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+  return launch_meta3_pack(meta, out, n_int16 / 8, err_count, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sm100_marlin_meta3_unpack(const void* in, void* out, int64_t n_int32, void* stream) {
@@ -990,14 +883,7 @@ int sm100_marlin_meta3_unpack(const void* in, void* out, int64_t n_int32, void* 
   if (!in || !out) return SM100_MARLIN_ERR_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(in) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u))
     return SM100_MARLIN_ERR_ALIGNMENT;
-  const int64_t lanes = n_int32 / 48 * 32;
-  const int threads = 256;
-  const int64_t blocks = (lanes + threads - 1) / threads;
-  meta3_unpack_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                        reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint32_t*>(in), static_cast<uint32_t*>(out), lanes);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+  return launch_meta3_unpack(in, out, n_int32 / 48 * 32, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sm100_marlin_meta3_decode_words(const void* in, void* out_high, void* out_low, int64_t n,
@@ -1005,14 +891,7 @@ int sm100_marlin_meta3_decode_words(const void* in, void* out_high, void* out_lo
   if (n < 0) return SM100_MARLIN_ERR_ARGUMENT;
   if (n == 0) return SM100_MARLIN_OK;
   if (!in || !out_high || !out_low) return SM100_MARLIN_ERR_ARGUMENT;
-  const int threads = 256;
-  const int64_t blocks = (n + threads - 1) / threads;
-  meta3_decode_words_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                              reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint32_t*>(in), static_cast<uint32_t*>(out_high),
-      static_cast<uint32_t*>(out_low), n);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+  return launch_meta3_decode_words(in, out_high, out_low, n, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sm100_marlin_device_status(int dev, int* status) {
@@ -1055,28 +934,8 @@ int sm100_marlin_pack_2_4(const void* w, const void* s, int prob_k, int prob_m, 
   if (!w || !s || !B || !meta || !s_out) return SM100_MARLIN_ERR_ARGUMENT;
   DeviceGuard guard(dev);
   if (!guard.ok) return cuda_fail(cudaGetLastError());
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_v);
-  const int g_rows = groupsize == -1 ? prob_k : groupsize;
-  const int s_rows = prob_k / g_rows;
-  auto blocks = [](long long total) {
-    const long long b = (total + 255) / 256;
-    return static_cast<int>(b < 148 * 16 ? b : 148 * 16);
-  };
-  const long long b_words = static_cast<long long>(prob_k / 32) * 2 * prob_m;
-  const long long meta_words = static_cast<long long>(prob_m) * (prob_k / 16);
-  const long long s_words = static_cast<long long>(s_rows) * prob_m;
-  pack_b_kernel<<<blocks(b_words), 256, 0, stream>>>(static_cast<const half*>(w),
-                                                     static_cast<const half*>(s), prob_k, prob_m,
-                                                     g_rows, static_cast<uint32_t*>(B));
-  pack_meta_kernel<<<blocks(meta_words), 256, 0, stream>>>(static_cast<const half*>(w),
-                                                           static_cast<const half*>(s), prob_k,
-                                                           prob_m, g_rows,
-                                                           static_cast<uint16_t*>(meta));
-  pack_scales_kernel<<<blocks(s_words), 256, 0, stream>>>(static_cast<const half*>(s), s_rows, prob_m,
-                                                          groupsize != -1 ? 1 : 0,
-                                                          static_cast<half*>(s_out));
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+  return launch_pack_2_4(w, s, prob_k, prob_m, groupsize, B, meta, s_out,
+                         reinterpret_cast<cudaStream_t>(stream_v));
 }
 
 int sm100_marlin_mul_2_4_gather(const void* A, const void* B, const void* meta, const void* s,

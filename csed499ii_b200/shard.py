@@ -25,7 +25,7 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["column_range", "slice_packed", "gather_columns", "mul_2_4_sharded", "ShardedWeight",
-           "FusedGather", "mul_2_4_gathered"]
+           "FusedGather", "mul_2_4_gathered", "check_status"]
 
 
 def column_range(n_out: int, rank: int, world: int) -> Tuple[int, int]:
@@ -199,10 +199,35 @@ class FusedGather:
             self._own = 0
 
 
-def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather):
+GATHER_WAIT_TIMEOUT = 8  # SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT
+
+
+def check_status(dev: int) -> None:
+    """Raise if a kernel on ``dev`` gave up a bounded wait since the last check.
+
+    Synchronises the device (reads and clears the library's status word).  A
+    fused all-gather whose peers did not all arrive in time sets
+    ``GATHER_WAIT_TIMEOUT``: its output then lacks some ranks' blocks.
+    """
+    from . import _ext
+
+    status = _ext.device_status(dev)
+    if status & GATHER_WAIT_TIMEOUT:
+        raise RuntimeError(f"fused all-gather timed out waiting for other ranks (status {status})")
+    if status:
+        raise RuntimeError(f"a GEMM kernel gave up a bounded wait (status {status})")
+
+
+def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather,
+                     check: bool = False):
     """``A @ W`` for the column-sharded W with the all-gather fused into the
     GEMM: returns this rank's ``(M, world * N/world)`` fp16 result (a view of
-    the fused buffer, valid until the call after next)."""
+    the fused buffer, valid until the call after next).
+
+    The call is asynchronous.  A rank whose peers do not arrive within the
+    kernel's wait limit gets an incomplete result and a device status bit;
+    ``check=True`` synchronises and raises in that case (otherwise call
+    :func:`check_status` at a synchronisation point of your own)."""
     from . import _ext, _groupsize, _stream_ptr
 
     m, k = A.shape
@@ -220,4 +245,6 @@ def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather)
         gather._c[buf], gather._flag[buf], gather._seen[buf], gather.world, gather.rank)
     if err != _ext.OK:
         raise RuntimeError(f"fused sharded GEMM failed: {_ext.describe(err)}")
+    if check:
+        check_status(dev)
     return gather.output(buf, m, cols)

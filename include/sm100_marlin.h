@@ -127,14 +127,38 @@ int sm100_marlin_mul_2_4_epilogue(const void* A, const void* B, const void* meta
  * Arguments and results are those of sm100_marlin_mul_2_4.
  * The first call on a device looks up the buffer's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture.  All noalloc calls on a device share the buffer:
- * calls that overlap on the GPU (different streams, no ordering between
- * them) race and must be avoided; calls on one stream are safe.
+ * before any stream capture.  The address stays cached for the life of the
+ * process: after cudaDeviceReset on a device (which destroys the buffer with
+ * the context) this entry point must not be used on that device again.  All
+ * noalloc calls on a device share the buffer: calls that overlap on the GPU
+ * (different streams, no ordering between them) race and must be avoided;
+ * calls on one stream are safe.
  */
 int sm100_marlin_mul_2_4_noalloc(const void* A, const void* B, const void* meta, void* C,
                                  const void* s, int prob_m, int prob_n, int prob_k,
                                  void* workspace, int groupsize, int dev, void* stream,
                                  int thread_k, int thread_m, int sms, int max_par);
+
+/*
+ * Metadata-cost diagnostics: mul_2_4 (4-bit metadata, group-128 scales) with
+ * the metadata path partly removed, to measure what it costs.  Replaces the
+ * reference's `metadata_diagnostics` extension and its `no_gmem` / `no_reg`
+ * / `no_all` kernels (kernel_experiments/sparse_marlin/kernel_profile/
+ * setup.py:14-38, driven by run.py:62-70).
+ *   variant 1  "no_gmem": no metadata copy from global memory; the kernel's
+ *              shared-memory metadata is the constant 0xEEEE from its start
+ *   variant 2  "no_reg": metadata copied as usual, but the constant 0xEEEE is
+ *              used in place of the shared-memory (or tensor-memory) load
+ *   variant 3  "no_all": both
+ * The result is only meaningful, and then bit-identical to mul_2_4, when every
+ * metadata word of `meta` is 0xEEEE (int16 -4370).  Runs the decode kernel for
+ * prob_n <= 64 and the CTA-pair tensor-memory kernel above (prob_m % 256 ==
+ * 0).  SM100_MARLIN_ERR_ARGUMENT for another variant or groupsize -1.
+ */
+int sm100_marlin_mul_2_4_meta_diag(const void* A, const void* B, const void* meta, void* C,
+                                   const void* s, int prob_m, int prob_n, int prob_k,
+                                   void* workspace, int groupsize, int dev, void* stream,
+                                   int variant);
 
 /*
  * Column-parallel GEMM with the all-gather of C fused into its epilogue.  No
@@ -203,7 +227,10 @@ int sm100_marlin_meta3_decode_words(const void* in, void* out_high, void* out_lo
                                     void* stream);
 
 /* Reads and clears the device status word of `dev` (synchronises the
- * device).  Nonzero bits mean a kernel gave up a bounded wait. */
+ * device).  Nonzero bits mean a kernel gave up a bounded wait.  The library
+ * looks up the word's device address once per device and keeps it for the
+ * life of the process, so none of its entry points may be used on a device
+ * after cudaDeviceReset there. */
 int sm100_marlin_device_status(int dev, int* status);
 
 /* Static description of a status code. */

@@ -10,6 +10,12 @@ Two generators, both built on the CPU oracle:
   positive scales); used for full-size shapes where packing from dense would
   dominate the test time.  Either way the oracle weight is
   ``dequant_2_4(B, meta, s)``.
+* :func:`packed_problem_gpu` + :func:`oracle_columns` -- the same kind of
+  inputs made on the GPU for layers too large for a whole-matrix numpy
+  oracle (Llama-2-70B); the oracle then dequantises a sample of 64-column
+  chunks, sliced from the packed tensors the way column shards are (every
+  permutation of the format stays inside a 64-column chunk; pinned bit-exact
+  by ``tests/test_shard.py``).
 """
 from __future__ import annotations
 
@@ -63,3 +69,54 @@ def errors(C, C_ref):
 # relative Frobenius error from the north-star statement.
 REL_MAE_TOL = 0.002
 REL_FRO_TOL = 1e-2
+
+
+def packed_problem_gpu(N: int, K: int, seed: int, sigma: float = 0.02, device: str = "cuda:0"):
+    """Random packed operator inputs made on the GPU: INT4 codes, legal 2:4
+    metadata nibbles, group-128 scales of the size absmax*2/15 gives for
+    weights ~N(0, sigma) (about 4.5 sigma * 2/15, +-50 %)."""
+    import torch
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    legal = torch.tensor([int(v) for v in LEGAL_NIBBLES], dtype=torch.int32, device=device)
+    B = torch.randint(-(2**31), 2**31 - 1, (K // 32, 2 * N), dtype=torch.int32, device=device,
+                      generator=gen)
+    idx = torch.randint(0, 6, (N * K // 16, 4), device=device, generator=gen)
+    nib = legal[idx]
+    meta = (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).to(torch.int16)
+    meta = meta.view(N, K // 16).contiguous()
+    del idx, nib
+    s = ((torch.rand((K // 128, N), device=device, generator=gen) + 0.5) * (4.5 * sigma * 2 / 15)).half()
+    return B, meta, s.contiguous()
+
+
+def sample_chunks(N: int, count: int = 8, seed: int = 0):
+    """Indices of `count` 64-column chunks: the first, the last and random ones."""
+    n = N // 64
+    rng = np.random.default_rng(seed)
+    inner = rng.permutation(np.arange(1, n - 1))[:max(0, count - 2)] if n > 2 else []
+    return sorted({0, n - 1} | set(int(c) for c in inner))
+
+
+def oracle_columns(B, meta, s, K: int, chunks):
+    """Oracle weight (K, 64*len(chunks)) of the given 64-column chunks, from
+    the packed tensors (torch or numpy) sliced per chunk."""
+    def host(t):
+        return t.cpu().numpy() if hasattr(t, "cpu") else np.asarray(t)
+
+    B, meta, s = host(B), host(meta), host(s)
+    kk = B.shape[0]
+    n_out = B.shape[1] // 2
+    parts = []
+    for c in chunks:
+        c0, c1 = 64 * c, 64 * c + 64
+        B_r = np.ascontiguousarray(B[:, 2 * c0:2 * c1])
+        meta_r = np.ascontiguousarray(meta.reshape(kk, n_out, 2)[:, c0:c1, :]).reshape(c1 - c0, 2 * kk)
+        s_r = np.ascontiguousarray(s[:, c0:c1])
+        parts.append(O.dequant_2_4(B_r, meta_r, s_r, K, c1 - c0, 128))
+    return np.concatenate(parts, axis=1)
+
+
+def chunk_columns(chunks):
+    return np.concatenate([np.arange(64 * c, 64 * c + 64) for c in chunks])

@@ -34,6 +34,50 @@ def test_pack_unpack_bit_exact_on_reference_metadata():
         assert torch.equal(restored.cpu(), torch.from_numpy(meta.reshape(-1)))
 
 
+def _reference_codec():
+    """The reference's own codec (metadata_decode/codec.cu), compiled from its
+    source by oracle/build_ref.py into oracle/_ref/ (a torch extension)."""
+    import glob
+    import importlib.machinery
+    import importlib.util
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    found = sorted(glob.glob(os.path.join(root, "oracle", "_ref", "ref_codec*.so")))
+    if not found:
+        pytest.skip("reference codec not built (oracle/build_ref.py needs the reference checkout)")
+    loader = importlib.machinery.ExtensionFileLoader("ref_codec", found[0])
+    spec = importlib.util.spec_from_loader("ref_codec", loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+def _legal_meta(n_int16, seed):
+    rng = np.random.default_rng(seed)
+    nib = rng.choice(np.array([0x4, 0x8, 0x9, 0xC, 0xD, 0xE], dtype=np.uint16), size=(n_int16, 4))
+    return (nib[:, 0] | (nib[:, 1] << 4) | (nib[:, 2] << 8) | (nib[:, 3] << 12)).astype(np.uint16).view(np.int16)
+
+
+def test_pack_bytes_equal_reference_codec():
+    """The packed 3-bit words are the reference codec's bytes, word for word
+    (not only a round trip of this library's own pack/unpack): on every golden
+    fixture's metadata and on one full 4096 x 4096 layer; and each side's
+    unpack inverts the other's pack (codec.cu:18-41, smoke.py:17-18)."""
+    from csed499ii_b200 import metadata_decode as md
+
+    ref = _reference_codec()
+    metas = [np.load(os.path.join(GOLDEN, name))["meta"].reshape(-1) for name in golden_cases()]
+    metas.append(_legal_meta(4096 * 4096 // 16, seed=5))
+    for meta in metas:
+        t = torch.from_numpy(np.ascontiguousarray(meta)).to(DEV)
+        ours = md.pack(t)
+        theirs = ref.pack(t)
+        torch.cuda.synchronize()
+        assert theirs.dtype == torch.int32 and torch.equal(ours, theirs)
+        assert torch.equal(md.unpack(theirs).view(-1), t)
+        assert torch.equal(ref.unpack(ours).view(-1), t)
+
+
 def test_pack_rejects_illegal_nibbles():
     from csed499ii_b200 import metadata_decode as md
 

@@ -61,6 +61,19 @@ def test_slice_equals_packing_the_slice():
     np.testing.assert_array_equal(s_r.numpy().view(np.uint16), s_p2.view(np.uint16))
 
 
+def test_oracle_columns_equals_whole_matrix_oracle():
+    # the column-sampled oracle of the large-layer GPU tests (problems.py)
+    # dequantises exactly the chosen columns of the whole-matrix oracle
+    from problems import chunk_columns, oracle_columns, sample_chunks
+
+    N, K = 1024, 512
+    W, B, s, meta = random_packed_problem(N, K, 128, seed=21)
+    chunks = sample_chunks(N, 5, seed=3)
+    assert chunks[0] == 0 and chunks[-1] == N // 64 - 1
+    part = oracle_columns(B, meta, s, K, chunks)
+    np.testing.assert_array_equal(part.view(np.uint16), W[:, chunk_columns(chunks)].view(np.uint16))
+
+
 def test_slice_of_3bit_metadata():
     N, K = 1024, 512
     _, B, s, meta = random_packed_problem(N, K, 128, seed=4)
