@@ -550,7 +550,20 @@ def bench_ablation(args, torch, dev, samples=9, graph_calls=100, replays=5):
     0xEEEE), every variant checked bit-exact against the baseline first, then
     `graph_calls` calls captured in one CUDA graph per variant, `samples`
     measurements of `replays` replays each in a shuffled order (seeded), and
-    the median per-call microseconds."""
+    the median per-call microseconds.  The diagnostics are instances of the
+    warp-level decode kernel and the CTA-pair kernel, so the baseline is
+    pinned to those (`sm100_marlin_set_decode_kernel(DECODE_STREAM_K)`)."""
+    from csed499ii_b200 import _ext
+
+    lib = _ext.load()
+    lib.sm100_marlin_set_decode_kernel(_ext.DECODE_STREAM_K)
+    try:
+        return _bench_ablation_pinned(torch, dev, samples, graph_calls, replays)
+    finally:
+        lib.sm100_marlin_set_decode_kernel(_ext.DECODE_AUTO)
+
+
+def _bench_ablation_pinned(torch, dev, samples, graph_calls, replays):
     import random
 
     import csed499ii_b200 as m

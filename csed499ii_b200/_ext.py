@@ -46,6 +46,7 @@ SIGNATURES = {
     "sm100_marlin_last_cuda_error": (ctypes.c_char_p, []),
     "sm100_marlin_set_trace_buffer": (_c_int, [_vp]),
     "sm100_marlin_set_overlap": (_c_int, [_c_int]),
+    "sm100_marlin_set_decode_kernel": (_c_int, [_c_int]),
     "sm100_marlin_pack_2_4": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                                        _vp]),
     "sm100_marlin_mul_2_4_gather": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
@@ -65,6 +66,10 @@ ERR_CUDA = 3
 ERR_ALIGNMENT = 4
 ERR_ARGUMENT = 5
 ERR_SCRATCH = 6
+
+DECODE_AUTO = 0
+DECODE_STREAM_K = 1
+DECODE_TMEM = 2
 
 
 _fast = None

@@ -37,6 +37,12 @@ enum : int {
 enum : int { kDiagNoGmem = 1, kDiagNoReg = 2 };
 constexpr uint32_t kDiagMetaWord = 0xEEEEEEEEu;
 
+// Timeline recording into a caller's buffer, compiled in only with
+// -DSM100_MARLIN_TRACE=1 (sm100_marlin_set_trace_buffer; off by default).
+#ifndef SM100_MARLIN_TRACE
+#define SM100_MARLIN_TRACE 0
+#endif
+
 // Upper bound for any single wait, in nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 500ull * 1000ull * 1000ull;
 
@@ -111,6 +117,50 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
   }
   return true;
+}
+
+// The same wait for warps that are not on the critical path: each poll
+// suspends the thread in hardware (suspend-time hint) until the phase
+// completes or ~20 us pass, so a waiting warp takes no issue slots from the
+// warps that share its sub-partition.  A poll of a completed phase costs ~50
+// cycles instead of ~15.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(uint32_t bar, uint32_t parity,
+                                                        volatile int* abort) {
+  unsigned long long t0 = 0;
+  while (!mbar_try_wait_sleep(bar, parity)) {
+    if (*abort) return false;
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// A critical-path wait that may also be long (e.g. for the previous kernel on
+// the stream): polls without a hint first, then sleeps in hardware between
+// polls so that a long wait takes no issue slots.
+__device__ __forceinline__ bool mbar_wait_spin_sleep_bounded(uint32_t bar, uint32_t parity,
+                                                             volatile int* abort) {
+#pragma unroll 1
+  for (int i = 0; i < 64; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_sleep_bounded(bar, parity, abort);
 }
 
 // ---------------------------------------------------------------------------
@@ -306,10 +356,12 @@ __device__ __forceinline__ void ldmatrix_x2(uint32_t (&r)[2], uint32_t addr) {
 //   lo(q) = (n0 - 8, n4 - 8)     hi(q) = (n1 - 8, n5 - 8)
 // where n_i is nibble i of q.
 // ---------------------------------------------------------------------------
+// A pure function of its operands: not volatile, so the compiler may schedule
+// and combine it like any other ALU operation.
 template <int LUT>
 __device__ __forceinline__ uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t r;
-  asm volatile("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(r) : "r"(a), "r"(b), "r"(c), "n"(LUT));
+  asm("lop3.b32 %0, %1, %2, %3, %4;" : "=r"(r) : "r"(a), "r"(b), "r"(c), "n"(LUT));
   return r;
 }
 

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "marlin24_decode_tc.cuh"
 #include "marlin24_gemm.cuh"
 #include "marlin24_prefill.cuh"
 
@@ -21,6 +22,15 @@ int cuda_fail(cudaError_t e);
 // One launch of the decode kernel (marlin24_gemm.cuh) on `grid` CTAs.
 template <int NC, int MB, int NH, bool META3, bool GROUPED, bool EPI, int DIAG>
 int launch_decode(const GemmParams& p, int grid, int dev, cudaStream_t stream);
+
+// One launch of the tensor-memory decode kernel (marlin24_decode_tc.cuh):
+// `grid` CTAs in clusters of p.split.
+template <int NR, bool META3, bool GROUPED>
+int launch_decode_tc(const DecodeTcParams& p, int grid, int dev, cudaStream_t stream);
+
+// Clusters of `split` CTAs (1 CTA per SM) of the tensor-memory decode kernel
+// that the device runs at once (0 on error).
+int decode_tc_max_clusters(int split, int dev);
 
 // Dense-expansion prefill kernel (marlin24_prefill.cuh).
 template <int BN, int NG, bool GROUPED>

@@ -5,6 +5,7 @@
 
 #include "../../include/sm100_marlin.h"
 #include "launch.cuh"
+#include "marlin24_decode_tc.cuh"
 #include "marlin24_prefill_sparse.cuh"
 
 namespace sm100 {
@@ -38,6 +39,38 @@ int launch_decode(const GemmParams& p, int grid, int dev, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
+}
+
+template <int NR, bool META3, bool GROUPED>
+int launch_decode_tc(const DecodeTcParams& p, int grid, int dev, cudaStream_t stream) {
+  using Cfg = DecodeTcCfg<NR, META3>;
+  static bool attr_set[64] = {};
+  auto kern = marlin24_decode_tc_kernel<NR, META3, GROUPED>;
+  int rc = set_smem_once(kern, Cfg::SMEM, attr_set, dev);
+  if (rc != SM100_MARLIN_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  ++na;
+  if (p.split > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = p.split;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) return cuda_fail(e);
   e = cudaGetLastError();

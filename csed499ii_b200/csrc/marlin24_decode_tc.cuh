@@ -1,0 +1,668 @@
+// 2:4 sparse W4A16 GEMM for batches of up to 64 rows on the tensor-memory
+// tensor cores (sm_100a): tcgen05.mma.sp kind::f16 with the COMPRESSED
+// weights as operand A read from tensor memory, activations as operand B
+// from shared memory, fp32 accumulators in tensor memory.
+//
+//   C[M, N] (fp16) = A[M, K] (fp16) . dequant(B, meta, s)[K, N]
+//
+// Inputs are the Sparse-Marlin packed layout (reference:
+// kernel_experiments/sparse_marlin/src/marlin/__init__.py:331-388 and
+// _semi_structured_conversions.py:54-179), 4-bit or 3-bit metadata
+// (kernel_experiments/sparse_marlin/metadata_decode/codec.cu:18-24).
+//
+// Work split.  Output features come in 128-feature blocks (one MMA's M).  A
+// cluster of S CTAs (S = 1, 2 or 4) owns `bpc` consecutive blocks and splits
+// K S ways: CTA r of the cluster streams K steps [r*ks/S, (r+1)*ks/S) of every
+// block of the cluster, block after block.  The S partial sums of a block are
+// reduced through distributed shared memory: CTA r owns rows
+// [r*128/S, (r+1)*128/S) of every block, every CTA sends it those rows of its
+// partial (st.async, counted on the owner's mbarrier), and the owner adds the
+// S partials in rank order (deterministic) and stores its part of C.  No
+// global scratch, no split-K counters: the workspace is never touched.
+//
+// Warp roles (16 warps, one CTA per SM).  Every single-thread issue of a TMA
+// copy, barrier wait, MMA or commit costs ~100-200 cycles on B200, so stages
+// are 256 K deep (8 MMAs of K = 32 per 128-feature block) and the issuing
+// roles are doubled:
+//   warps 0-1    TMA, stages in turn: the packed codes, metadata and scale
+//                rows of the block (before the programmatic-launch wait:
+//                weights do not depend on the previous kernel), then the
+//                activation slice.
+//   warps 2-3    MMA issue (one thread each), a block's stages in turn, each
+//                into its own accumulator (the epilogue adds the two in a
+//                fixed order); tensor-memory allocation.
+//   warps 4-11   dequantise, two groups of four taking the stages in turn:
+//                each thread owns one MMA row (one output feature): INT4
+//                codes -> fp16 (magic-number method), group scale applied,
+//                the 16 compressed values of each 32-K row written to its
+//                tensor-memory lane (tcgen05.st), and its metadata word
+//                copied (3-bit metadata decoded first).
+//   warps 12-15  epilogue: accumulators -> registers, the DSMEM exchange,
+//                sums and the 16-byte stores of C.
+// Two accumulator pairs alternate between consecutive blocks, so the
+// epilogue of one block overlaps the MMAs of the next.
+//
+// Row order.  MMA row m (tensor-memory lane m) of a block holds output feature
+// 32q + phi(l) of the block, q = m / 32, l = m % 32,
+//   phi(l) = 8 ((l & 7) >> 1) + 2 (l & 1) + (l >> 4) + 4 ((l >> 3) & 1).
+// Rows m and m + 8 (m % 16 < 8) are then features f and f + 4, whose 2:4
+// metadata share one packed 32-bit word per dense-K half, which is exactly
+// what one metadata lane of the sparse MMA holds (lane (m % 8) + 8h + 16(m/16):
+// row m in bits 0-15, row m + 8 in bits 16-31, for dense-K half h); the lane
+// -> feature map also spreads each warp's code-word loads over 8 banks, and
+// each 32-lane quarter covers 32 consecutive features.  Operand A in tensor
+// memory: row m at lane m, compressed K pair (2j, 2j+1) in 32-bit column j.
+// Both layouts were checked bit-exact against a CPU GEMM by a one-tile probe
+// before this kernel was written.
+#pragma once
+
+#include "marlin24_prefill_sparse.cuh"
+
+namespace sm100 {
+
+struct DecodeTcParams {
+  CUtensorMap tm_act;   // A fp16 (64, M, K/64), box (64, NR, 4), 128-byte swizzle
+  CUtensorMap tm_b;     // B u64 (N, K/32), box (128, 8): one block's codes, 8 rows of 32 K
+  CUtensorMap tm_meta;  // meta u64 (N/2 or 3N/8, K/32), box (64 or 48, 8)
+  CUtensorMap tm_s;     // s u64 (N/4, K/128), box (32, 2)  (grouped only)
+  const uint8_t* s;     // fp16 scales (per-column mode: applied in the epilogue)
+  half* C;              // fp16 (M, N) row-major
+  const half* bias;     // fused epilogue: fp16 per output column, or null
+  int act;              // fused epilogue activation (kAct*)
+  int* status;          // device status word
+  int M;
+  int N;
+  int ksteps;           // K / 256 (stages per block)
+  int split;            // S: CTAs of a cluster splitting K (1, 2 or 4)
+  int bpc;              // 128-feature blocks per cluster
+  int nblocks;          // N / 128
+  int pdl;              // launched with programmatic dependent launch
+  unsigned long long* trace;  // per-stage clock64 stamps of CTA 0 (SM100_MARLIN_TRACE builds)
+};
+
+// Trace builds (-DSM100_MARLIN_TRACE=1): CTA 0 records, per stage s < 64,
+// words [16s + i]: 0 producer issue, 1 dequant start (weights landed),
+// 2 dequant done (tensor memory written), 3 MMA start (operands ready),
+// 4 MMA issued, 5 epilogue got the block's accumulator (first stage of the
+// block's slot), 6 epilogue stored C, 8-14 inside the MMA warp's step (loop
+// top, tensor stage ready, activations ready, after the fence, after the
+// first and the last MMA, after the commits); word 1024 the CTA's clock at
+// entry.
+constexpr int kTcTraceStages = 64;
+constexpr int kTcTraceWords = 16;
+
+template <int NR, bool META3>
+struct DecodeTcCfg {
+  static_assert(NR == 16 || NR == 32 || NR == 48 || NR == 64, "batch tile");
+  static constexpr int KS = 2;                         // 128-K sub-steps per stage (256 K)
+  static constexpr int SMEM_BUDGET = 227 * 1024;       // one CTA per SM
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int ACT = 2 * KS * NR * 128;        // 64-K atoms of NR rows
+  static constexpr int CODES = KS * 4 * 1024;          // 32-K rows x 2 chunks x 512 B
+  static constexpr int META_ROW = META3 ? 384 : 512;   // per 32-K row, both chunks
+  static constexpr int META = KS * 4 * META_ROW;
+  static constexpr int SCALES = KS * 256;
+  static constexpr int OFF_ACT = 0;                    // 1024-aligned (swizzle atoms)
+  static constexpr int OFF_B = ACT;
+  static constexpr int OFF_M = OFF_B + CODES;
+  static constexpr int OFF_S = OFF_M + META;
+  static constexpr int STAGE = (OFF_S + SCALES + 1023) / 1024 * 1024;
+  static constexpr int HEADER = 1024;
+  static constexpr int RECV = 128 * NR * 4;            // one exchange buffer
+  static constexpr int OFF_RECV = HEADER;
+  static constexpr int OFF_RING = HEADER + 2 * RECV;
+  // Both rings have an even depth: the two TMA warps, the two dequantising
+  // groups and the two MMA warps take stages by parity, so each then owns a
+  // fixed half of the slots and waits on a slot only after it waited on the
+  // slot's previous use (a barrier waited on by phase parity must never be
+  // two phases behind its waiter).
+  static constexpr int DS_FIT = (SMEM_BUDGET - OFF_RING - 1024) / STAGE;
+  static constexpr int DS = (DS_FIT > 12 ? 12 : DS_FIT) & ~1;  // shared-memory stages
+  static constexpr int SMEM = OFF_RING + DS * STAGE + 1024;
+  // tensor memory: per stage 8 MMAs x (8 A + 4 metadata) columns; two
+  // accumulators (consecutive blocks) for each of the two MMA-issuing warps
+  static constexpr int TSLOT = KS * 48;
+  static constexpr int MMA_WARPS = 2;
+  static constexpr int ACC_COLS = MMA_WARPS * 2 * NR;
+  static constexpr int DT_FIT = (TMEM_COLS - ACC_COLS) / TSLOT;
+  static constexpr int DT = (DT_FIT > 4 ? 4 : DT_FIT) & ~1;    // tensor-memory stages
+  // warps: 0-1 TMA, 2-3 MMA, then DG groups of four dequantising warps, then
+  // four epilogue warps
+  static constexpr int DG = 2;
+  static constexpr int WARP_MMA = 2;
+  static constexpr int WARP_DQ = 4;
+  static constexpr int WARP_EPI = WARP_DQ + 4 * DG;
+  static constexpr int THREADS = (WARP_EPI + 4) * 32;
+  static_assert(DS >= 2 && DT >= 2 && DS % 2 == 0 && DT % 2 == 0, "ring depths");
+  static_assert((3 * DS + 2 * DT + 8) * 8 <= 1000, "barriers exceed the header");
+};
+
+// Row m = 32q + l of a block holds feature 32q + phi(l) (see the file comment).
+__device__ __forceinline__ int tc_row_feature(int l) {
+  return 8 * ((l & 7) >> 1) + 2 * (l & 1) + (l >> 4) + 4 * ((l >> 3) & 1);
+}
+
+__device__ __forceinline__ void tmem_st32_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The sparse MMA with operand A in tensor memory.
+__device__ __forceinline__ void umma_sp_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                               uint32_t e_tmem, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.sp.cta_group::1.kind::f16 [%0], [%1], %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 16 bytes into another CTA's shared memory (shared::cluster address), the
+// bytes counted on that CTA's mbarrier (shared::cluster address).
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, const float4& v, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          cluster_addr),
+      "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+      "r"(__float_as_uint(v.w)), "r"(cluster_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, const float4& v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint16_t lds16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// INT4 -> fp16 pair, the magic-number method of dequant_pair in plain C++
+// (no volatile asm): the compiler fuses the masks into LOP3s and is free to
+// schedule the 16 independent word chains of a stage together.
+__device__ __forceinline__ void dequant_pair_sched(uint32_t q, half2& lo, half2& hi) {
+  const uint32_t l = (q & 0x000f000fu) | 0x64006400u;
+  const uint32_t h = (q & 0x00f000f0u) | 0x64006400u;
+  const uint32_t kSub = 0x64086408u;  // (1032, 1032)
+  const uint32_t kMul = 0x2c002c00u;  // (1/16, 1/16)
+  const uint32_t kAdd = 0xd480d480u;  // (-72, -72)
+  lo = __hsub2(*reinterpret_cast<const half2*>(&l), *reinterpret_cast<const half2*>(&kSub));
+  hi = __hfma2(*reinterpret_cast<const half2*>(&h), *reinterpret_cast<const half2*>(&kMul),
+               *reinterpret_cast<const half2*>(&kAdd));
+}
+
+template <int NR, bool META3, bool GROUPED>
+__global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
+    marlin24_decode_tc_kernel(const __grid_constant__ DecodeTcParams p) {
+  using Cfg = DecodeTcCfg<NR, META3>;
+  constexpr int DS = Cfg::DS;
+  constexpr int DT = Cfg::DT;
+  constexpr int KS = Cfg::KS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* sfull = reinterpret_cast<uint64_t*>(smem);  // codes/meta/scales landed (1 + tx)
+  uint64_t* afull = sfull + DS;                         // activations landed (1 + tx)
+  uint64_t* sempty = afull + DS;                        // stage free (4 dequant warps + MMA commit)
+  uint64_t* tready = sempty + DS;                       // tensor-memory stage written (4 warps)
+  uint64_t* tempty = tready + DT;                       // tensor-memory stage consumed (commit)
+  uint64_t* accfull = tempty + DT;                      // accumulators complete (MMA warps' commits)
+  uint64_t* accempty = accfull + 2;                     // accumulators read out (4 epilogue warps)
+  uint64_t* recvb = accempty + 2;                       // exchange buffer filled (1 + tx)
+  uint64_t* freeb = recvb + 2;                          // exchange buffers released (S owners)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::HEADER - 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::HEADER - 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned long long* const trace = (SM100_MARLIN_TRACE && p.trace && blockIdx.x == 0) ? p.trace : nullptr;
+  if (trace && threadIdx.x == 0) trace[kTcTraceWords * kTcTraceStages] = clock64();
+  auto stamp = [&](int s, int i) {
+    if (trace && lane == 0 && s < kTcTraceStages) trace[kTcTraceWords * s + i] = clock64();
+  };
+  const int S = p.split;
+  const uint32_t rank = S > 1 ? cluster_cta_rank() : 0u;
+  const int b0 = static_cast<int>(blockIdx.x) / S * p.bpc;
+  const int nb = min(b0 + p.bpc, p.nblocks) - b0;  // blocks of this cluster (>= 1)
+  const int k_lo = static_cast<int>(rank) * p.ksteps / S;
+  const int kn = (static_cast<int>(rank) + 1) * p.ksteps / S - k_lo;  // stages per block (>= 1)
+  const int T = nb * kn;                                              // stages of this CTA
+  // MMA warp w takes the stages s with s % 2 == w (with one stage per block,
+  // warp 0 takes them all: every block's accumulator then has one writer)
+  const int mma_warps = kn >= 2 ? 2 : 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DS; ++i) {
+      mbar_init(smem_addr(&sfull[i]), 1);
+      mbar_init(smem_addr(&afull[i]), 1);
+      mbar_init(smem_addr(&sempty[i]), 5);
+    }
+    for (int i = 0; i < DT; ++i) {
+      mbar_init(smem_addr(&tready[i]), 4);
+      mbar_init(smem_addr(&tempty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&accfull[i]), mma_warps);
+      mbar_init(smem_addr(&accempty[i]), 4);
+      mbar_init(smem_addr(&recvb[i]), 1);
+      mbar_init(smem_addr(&freeb[i]), S);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&p.tm_act);
+    prefetch_tmap(&p.tm_b);
+    prefetch_tmap(&p.tm_meta);
+    if (GROUPED) prefetch_tmap(&p.tm_s);
+  }
+  if (warp == Cfg::WARP_MMA) tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
+  // let the next kernel on the stream start streaming its weights
+  if (p.pdl && threadIdx.x == 0) grid_dependency_launch();
+  tc_fence_before();
+  if (S > 1)
+    cluster_sync_all();  // peers' barriers exist before any remote arrive or st.async
+  else
+    __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t ring = smem_addr(smem + Cfg::OFF_RING);
+
+  if (warp < Cfg::WARP_MMA) {
+    // ------------------------------------------------------------- TMA issue
+    // Two warps take the stages in turn (one warp issues a stage's four
+    // copies in ~700 cycles); lane 0 issues.  Weight parts of the first
+    // stages go out before griddepcontrol.wait, activation parts after it.
+    const int pw = warp;
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
+    const uint32_t tx_w = Cfg::CODES + Cfg::META + (GROUPED ? Cfg::SCALES : 0);
+    bool waited = p.pdl == 0;
+    int n_pend = 0;
+    int pend_slot[DS / 2 + 1], pend_ks[DS / 2 + 1];
+    auto issue_act = [&](int slot, int ks) {
+      const uint32_t af = smem_addr(&afull[slot]);
+      mbar_arrive_expect_tx(af, Cfg::ACT);
+      tma_load_3d(ring + slot * Cfg::STAGE + Cfg::OFF_ACT, &p.tm_act, 0, 0, 2 * KS * ks, af, pol_keep);
+    };
+    int b = b0, ks = k_lo;
+    if (pw == 1 && T > 1) {  // start at stage 1
+      if (++ks == k_lo + kn) {
+        ks = k_lo;
+        ++b;
+      }
+    }
+    for (int s = pw; s < T && !*abort_flag; s += 2) {
+      const int slot = s % DS;
+      if (s >= DS) {
+        if (!waited) {  // a stage frees only after its MMAs, which need the activations
+          grid_dependency_wait();
+          waited = true;
+          if (lane == 0)
+            for (int i = 0; i < n_pend; ++i) issue_act(pend_slot[i], pend_ks[i]);
+          n_pend = 0;
+        }
+        const bool ok = mbar_wait_sleep_bounded(smem_addr(&sempty[slot]), ((s / DS) - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) atomicOr(p.status, kStatusEmptyWaitTimeout);
+          break;
+        }
+      }
+      stamp(s, 0);
+      if (lane == 0) {
+        const uint32_t st = ring + slot * Cfg::STAGE;
+        const uint32_t sf = smem_addr(&sfull[slot]);
+        mbar_arrive_expect_tx(sf, tx_w);
+        tma_load_2d(st + Cfg::OFF_B, &p.tm_b, b * 128, ks * 4 * KS, sf, pol_stream);
+        tma_load_2d(st + Cfg::OFF_M, &p.tm_meta, b * (META3 ? 48 : 64), ks * 4 * KS, sf, pol_stream);
+        if (GROUPED) tma_load_2d(st + Cfg::OFF_S, &p.tm_s, b * 32, ks * KS, sf, pol_keep);
+        if (waited) {
+          issue_act(slot, ks);
+        } else {
+          pend_slot[n_pend] = slot;
+          pend_ks[n_pend] = ks;
+        }
+      }
+      if (!waited) ++n_pend;
+      __syncwarp();
+      // advance two stages
+      for (int a = 0; a < 2; ++a)
+        if (++ks == k_lo + kn) {
+          ks = k_lo;
+          ++b;
+        }
+    }
+    if (!waited) {
+      grid_dependency_wait();
+      if (lane == 0)
+        for (int i = 0; i < n_pend; ++i) issue_act(pend_slot[i], pend_ks[i]);
+    }
+  } else if (warp < Cfg::WARP_DQ) {
+    // ------------------------------------------------------------- MMA issue
+    // Two warps, one thread each, take the stages in turn, each accumulating
+    // into its own accumulator: one warp's barrier waits and commits (100-200
+    // cycles each) overlap the other's MMAs.  The epilogue adds the two
+    // accumulators in a fixed order.
+    const int w = warp - Cfg::WARP_MMA;
+    constexpr uint32_t idesc = umma_idesc_f16_f32(NR) | (1u << 2);  // sparse
+    constexpr uint64_t kAtom = (NR * 128) >> 4;                     // next 64-K atom
+    if (w < mma_warps) {
+      int j = 0, i_in = 0, slot = 0, t = 0;
+      uint32_t sph = 0, tph = 0;  // phase parities of slot / t
+      bool first = true;          // this warp's first stage of block j
+      for (int s = 0; s < T; ++s) {
+        if ((s & 1) == w || mma_warps == 1) {
+          bool ok = true;
+          stamp(s, 8);
+          if (first && j >= 2)  // the epilogue has read this accumulator out
+            ok = mbar_wait_spin_sleep_bounded(smem_addr(&accempty[j & 1]), ((j >> 1) - 1) & 1, abort_flag);
+          ok = ok && mbar_wait_spin_sleep_bounded(smem_addr(&tready[t]), tph, abort_flag);
+          stamp(s, 9);
+          ok = ok && mbar_wait_spin_sleep_bounded(smem_addr(&afull[slot]), sph, abort_flag);
+          stamp(s, 10);
+          if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
+            break;
+          }
+          tc_fence_after();
+          stamp(s, 3);
+          if (lane == 0) {
+            const uint32_t acc = tmem + (w * 2 + (j & 1)) * NR;
+            const uint32_t ta = tmem + Cfg::ACC_COLS + t * Cfg::TSLOT;
+            const uint64_t bd = umma_desc_sw128_k(ring + slot * Cfg::STAGE + Cfg::OFF_ACT);
+#pragma unroll
+            for (int i = 0; i < 4 * KS; ++i)
+              umma_sp_f16_ts(acc, ta + 8 * i, bd + (i >> 1) * kAtom + (i & 1) * 4,
+                             ta + 32 * KS + 4 * i, idesc, (first && i == 0) ? 0u : 1u);
+            stamp(s, 13);
+            umma_commit(smem_addr(&tempty[t]));
+            umma_commit(smem_addr(&sempty[slot]));
+            // this warp's last stage of the block
+            if (i_in + mma_warps >= kn) umma_commit(smem_addr(&accfull[j & 1]));
+          }
+          stamp(s, 4);
+          __syncwarp();
+          first = false;
+        }
+        if (++slot == DS) {
+          slot = 0;
+          sph ^= 1u;
+        }
+        if (++t == DT) {
+          t = 0;
+          tph ^= 1u;
+        }
+        if (++i_in == kn) {
+          i_in = 0;
+          ++j;
+          first = true;
+        }
+      }
+    }
+  } else if (warp < Cfg::WARP_EPI) {
+    // -------------------------------------------------------------- dequantise
+    const int q = warp & 3;                       // tensor-memory lanes 32q .. 32q+31
+    const int grp = (warp - Cfg::WARP_DQ) >> 2;   // stages s % DG == grp
+    const int l = lane;
+    const int c = q >> 1;                           // 64-feature chunk of the block
+    const int g = 4 * (q & 1) + ((l & 7) >> 1);     // 8-feature group in the chunk
+    const int jp = 2 * (l & 1) + (l >> 4);          // feature in the group (and +4)
+    const int e = (l >> 3) & 1;                     // 0: feature 8g + jp, 1: + 4
+    // code words 16g + 4t + jp of chunk c (t = 0..3), nibbles of this feature
+    const uint32_t code_off = Cfg::OFF_B + c * 512 + 4 * (16 * g + jp);
+    const uint32_t scale_off = Cfg::OFF_S + 2 * (64 * c + 8 * g + 2 * jp + e);
+    // metadata word of this lane: pair (f, f + 4), dense-K half e
+    const int w4 = 32 * (l & 1) + 4 * g + 2 * (l >> 4) + e;
+    const uint32_t meta_off = META3 ? (Cfg::OFF_M + c * 192 + 4 * (w4 & 31))
+                                    : (Cfg::OFF_M + c * 256 + 4 * w4);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * q) << 16) + Cfg::ACC_COLS;
+    for (int s = grp; s < T; s += Cfg::DG) {
+      const int slot = s % DS;
+      const int t = s % DT;
+      bool ok = mbar_wait_sleep_bounded(smem_addr(&sfull[slot]), (s / DS) & 1, abort_flag);
+      if (s >= DT)
+        ok = ok && mbar_wait_sleep_bounded(smem_addr(&tempty[t]), ((s / DT) - 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
+        break;
+      }
+      tc_fence_after();
+      if (q == 0) stamp(s, 1);
+      const uint8_t* stp = smem + Cfg::OFF_RING + slot * Cfg::STAGE;
+      const uint32_t tslot = lane_base + t * Cfg::TSLOT;
+#pragma unroll
+      for (int h = 0; h < KS; ++h) {
+        // plain loads (ordered after the barrier wait by its memory clobber),
+        // all issued before any use so that their latencies overlap
+        uint32_t words[16];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int tt = 0; tt < 4; ++tt)
+            words[kk * 4 + tt] = *reinterpret_cast<const uint32_t*>(
+                stp + code_off + (4 * h + kk) * 1024 + 16 * tt);
+        uint32_t mraw[META3 ? 8 : 4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mraw[kk] = *reinterpret_cast<const uint32_t*>(stp + meta_off + (4 * h + kk) * Cfg::META_ROW);
+          if constexpr (META3)
+            mraw[4 + kk] = *reinterpret_cast<const uint32_t*>(stp + meta_off + (4 * h + kk) * Cfg::META_ROW + 64);
+        }
+        half2 s2 = __float2half2_rn(1.f);
+        if (GROUPED) {
+          const half sh = *reinterpret_cast<const half*>(stp + scale_off + 256 * h);
+          s2 = __halves2half2(sh, sh);
+        }
+        uint32_t v[32];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int tt = 0; tt < 4; ++tt) {
+            const uint32_t wd = words[kk * 4 + tt];
+            half2 lo, hi;
+            dequant_pair_sched(e ? (wd >> 8) : wd, lo, hi);  // (kc 2tt, 2tt+1), (kc 8+2tt, 9+2tt)
+            if (GROUPED) {
+              lo = __hmul2(lo, s2);
+              hi = __hmul2(hi, s2);
+            }
+            v[kk * 8 + tt] = *reinterpret_cast<uint32_t*>(&lo);
+            v[kk * 8 + 4 + tt] = *reinterpret_cast<uint32_t*>(&hi);
+          }
+        }
+        uint32_t mw[4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          if constexpr (META3) {
+            // 4-bit word w4 of the chunk is the high (w4 < 32) or low decode of
+            // 3-bit words w4 % 32 and w4 % 32 + 16 (meta3_pair_decode)
+            const uint32_t a = mraw[kk], bb = mraw[4 + kk];
+            const bool upper = (w4 & 31) >= 16;
+            if (w4 >= 32)
+              mw[kk] = decode24_low(upper ? (bb >> 8) : __funnelshift_r(a, bb, 24));
+            else
+              mw[kk] = decode24_high(upper ? __funnelshift_r(a, bb, 16) : a);
+          } else {
+            mw[kk] = mraw[kk];
+          }
+        }
+        tmem_st32_x32(tslot + 32 * h, v);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tmem_st32(tslot + 32 * KS + 16 * h + 4 * kk, mw[kk]);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_addr(&tready[t]));
+        mbar_arrive(smem_addr(&sempty[slot]));
+      }
+      if (q == 0) stamp(s, 2);
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int row = 32 * q + lane;                   // accumulator lane
+    const int feat = 32 * q + tc_row_feature(lane);  // feature of that row in the block
+    const int slice = 128 / S;                       // rows (features) each CTA owns
+    const uint32_t owner = static_cast<uint32_t>(row / slice);
+    const int et = threadIdx.x - Cfg::WARP_EPI * 32;  // 0 .. 127
+    const uint32_t recv = smem_addr(smem + Cfg::OFF_RECV);
+    const uint32_t lane_acc = tmem + (static_cast<uint32_t>(32 * q) << 16);
+    // C may still be read by the previous kernel on the stream
+    if (p.pdl) grid_dependency_wait();
+    for (int j = 0; j < nb; ++j) {
+      const int buf = j & 1;
+      bool ok = mbar_wait_sleep_bounded(smem_addr(&accfull[buf]), (j >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
+        break;
+      }
+      tc_fence_after();
+      if (q == 0) stamp(j * kn, 5);
+      // sum of the MMA warps' accumulators, warp 0 first
+      uint32_t r[NR];
+      float acc[NR];
+#pragma unroll
+      for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + buf * NR + c0, r + c0);
+      tmem_wait_ld();
+#pragma unroll
+      for (int u = 0; u < NR; ++u) acc[u] = __uint_as_float(r[u]);
+      if (mma_warps == 2) {
+#pragma unroll
+        for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + (2 + buf) * NR + c0, r + c0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < NR; ++u) acc[u] += __uint_as_float(r[u]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&accempty[buf]));
+      // every owner has released exchange buffer `buf` (block j - 2)
+      if (S > 1 && j >= 2) {
+        ok = mbar_wait_sleep_bounded(smem_addr(&freeb[buf]), ((j >> 1) - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
+          break;
+        }
+      }
+      // this row of the partial -> its owner's buffer, at [rank][feature in slice]
+      const uint32_t dst = recv + buf * Cfg::RECV +
+                           ((rank * slice + (feat - static_cast<int>(owner) * slice)) * NR) * 4;
+      if (S > 1) {
+        const uint32_t rdst = mapa_shared(dst, owner);
+        const uint32_t rbar = mapa_shared(smem_addr(&recvb[buf]), owner);
+#pragma unroll
+        for (int c0 = 0; c0 < NR; c0 += 4)
+          st_async_v4(rdst + 4 * c0, make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]), rbar);
+        if (et == 0) mbar_arrive_expect_tx(smem_addr(&recvb[buf]), Cfg::RECV);
+        ok = mbar_wait_sleep_bounded(smem_addr(&recvb[buf]), (j >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
+          break;
+        }
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < NR; c0 += 4)
+          sts128(dst + 4 * c0, make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]));
+      }
+      named_bar_sync(1, 128);
+      // sums of this CTA's slice: 8 features x 1 batch row per item, the S
+      // partials added in rank order; 16-byte stores of C
+      const int n0 = (b0 + j) * 128 + static_cast<int>(rank) * slice;
+      const int groups = slice / 8;
+      for (int it = et; it < groups * p.M; it += 128) {
+        const int rr = it / groups;
+        const int fg = it - rr * groups;
+        float sum[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sum[u] = 0.f;
+        for (int src = 0; src < S; ++src) {
+          const uint32_t base = recv + buf * Cfg::RECV + ((src * slice + fg * 8) * NR + rr) * 4;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) sum[u] += lds_f32(base + u * NR * 4);
+        }
+        const int n = n0 + fg * 8;
+        if (!GROUPED) {
+          const uint4 sv = *reinterpret_cast<const uint4*>(p.s + 2ll * n);
+          const half2* sh = reinterpret_cast<const half2*>(&sv);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            sum[2 * u] *= __low2float(sh[u]);
+            sum[2 * u + 1] *= __high2float(sh[u]);
+          }
+        }
+        if (p.bias != nullptr || p.act != kActNone) {
+          float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (p.bias != nullptr) {
+            const uint4 braw = *reinterpret_cast<const uint4*>(p.bias + n);
+            const half2* bh = reinterpret_cast<const half2*>(&braw);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              bv[2 * u] = __low2float(bh[u]);
+              bv[2 * u + 1] = __high2float(bh[u]);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) sum[u] = epilogue_act(sum[u] + bv[u], p.act);
+        }
+        uint4 o;
+        half2* oh = reinterpret_cast<half2*>(&o);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) oh[u] = __floats2half2_rn(sum[2 * u], sum[2 * u + 1]);
+        *reinterpret_cast<uint4*>(p.C + static_cast<long long>(rr) * p.N + n) = o;
+      }
+      named_bar_sync(1, 128);
+      if (q == 0) stamp(j * kn, 6);
+      // release buffer `buf` to every CTA of the cluster (needed only when a
+      // block j + 2 follows)
+      if (S > 1 && j + 2 < nb && et < S)
+        mbar_arrive_remote(mapa_shared(smem_addr(&freeb[buf]), static_cast<uint32_t>(et)));
+    }
+  }
+
+  // Teardown: all MMAs complete before the tensor memory is released, and no
+  // CTA of the cluster leaves while a peer may still write to its shared
+  // memory.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == Cfg::WARP_MMA && *abort_flag == 0)  // the last block's accumulators are complete
+    mbar_wait_sleep_bounded(smem_addr(&accfull[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort_flag);
+  tc_fence_before();
+  if (S > 1)
+    cluster_sync_all();
+  else
+    __syncthreads();
+  tc_fence_after();
+  if (warp == Cfg::WARP_MMA) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+}  // namespace sm100

@@ -99,9 +99,6 @@ constexpr int kTraceStages = 64;
 constexpr int kTraceStageWords = 8;
 // Words per launch in a trace buffer (grid <= 256 CTAs).
 constexpr long long kTraceLaunchWords = 256 * kTraceWords + kTraceStages * kTraceStageWords;
-#ifndef SM100_MARLIN_TRACE
-#define SM100_MARLIN_TRACE 0
-#endif
 
 // Warp roles per configuration: 8 consumer warps; 2 producer warps for batch
 // rows <= 16 (24 KB weight stages) and 4 for larger batches (smaller stages).

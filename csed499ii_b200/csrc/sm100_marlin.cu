@@ -597,6 +597,11 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
 #undef SM100_PREFILL_SP2
     return SM100_MARLIN_ERR_KERN_SHAPE;
   }
+#if SM100_MARLIN_TUNING
+  // One CTA per 128-feature tile.  Unreachable with the default settings:
+  // batches above 16 rows need N % 256 == 0 (the reference's shape rule),
+  // which always allows CTA pairs; kept for experiments (knobs
+  // SM100_MARLIN_PREFILL_PAIR=0, SM100_MARLIN_PREFILL_BN=128).
 #define SM100_PREFILL_SP(BN_, NG_)                                                   \
   if (bn == BN_ && ng == NG_)                                                        \
     return p.grouped ? launch_prefill_sp<BN_, NG_, true>(p, dev, stream)        \
@@ -608,6 +613,7 @@ int mul_prefill_sparse(PrefillParams& p, const void* A, const void* B, const voi
   SM100_PREFILL_SP(256, 2)
   SM100_PREFILL_SP(256, 4)
 #undef SM100_PREFILL_SP
+#endif
   return SM100_MARLIN_ERR_KERN_SHAPE;
 }
 
@@ -662,6 +668,116 @@ int mul_prefill(const void* A, const void* B, const void* meta, void* C, const v
   return SM100_MARLIN_ERR_KERN_SHAPE;
 }
 
+// Which kernel takes batches of at most 64 rows (sm100_marlin_set_decode_kernel).
+int g_decode_kernel = SM100_MARLIN_DECODE_AUTO;
+
+// Whether a batch of `rows` (<= 64) goes to the tensor-memory decode kernel
+// (marlin24_decode_tc.cuh).  Its single-thread MMA issue costs the same at
+// 16 rows as at 64, so smaller batches stream faster on the warp-level kernel
+// (Llama-7B step, 4-bit: 1666 vs 2174 GB/s at 16 rows, 1544 vs 1338 at 32,
+// 973 vs 785 at 64; 3-bit: 990 vs 1156 at 32, 716 vs 679 at 64).
+bool decode_tc_rows(int rows, int meta_bits) {
+  if (g_decode_kernel == SM100_MARLIN_DECODE_TMEM) return true;
+  if (g_decode_kernel == SM100_MARLIN_DECODE_STREAM_K) return false;
+  return rows > (meta_bits == 3 ? 32 : 16);
+}
+
+// Plan: clusters of S CTAs (S = 1, 2, 4) split K S ways over `bpc`
+// consecutive 128-feature blocks each.  At most one CTA per SM (clusters of
+// four fit only 33 to a B200 that way), the fewest K steps per CTA wins;
+// ties go to the smaller cluster.
+struct TcPlan {
+  int split, bpc, clusters;
+};
+
+TcPlan plan_decode_tc(int n_out, int k_in, int sms, int dev) {
+  const int nblocks = n_out / 128, ksteps = k_in / 256;  // 256-K stages
+  TcPlan best{1, nblocks, 1};
+  long long best_cost = -1;
+  for (int split : {1, 2, 4}) {
+    if (ksteps < split) continue;
+    int maxcl = split == 1 ? sms : decode_tc_max_clusters(split, dev);
+    if (split > 1 && maxcl > sms / split) maxcl = sms / split;
+    if (maxcl <= 0) continue;
+    int cl = nblocks < maxcl ? nblocks : maxcl;
+    const int bpc = (nblocks + cl - 1) / cl;
+    cl = (nblocks + bpc - 1) / bpc;
+    const long long cost = static_cast<long long>(bpc) * ((ksteps + split - 1) / split);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = TcPlan{split, bpc, cl};
+    }
+  }
+  return best;
+}
+
+template <int NR, bool META3>
+int dispatch_decode_tc(const DecodeTcParams& p, int grid, int dev, cudaStream_t stream, bool grouped) {
+  return grouped ? launch_decode_tc<NR, META3, true>(p, grid, dev, stream)
+                 : launch_decode_tc<NR, META3, false>(p, grid, dev, stream);
+}
+
+// C[M, N] = A . dequant(B, meta, s) for M <= 64, N % 128 == 0, K % 256 == 0
+// on the tensor-memory decode kernel (stages of 256 K: 8 rows of 32 K).
+int mul_decode_tc(const void* A, const void* B, const void* meta, void* C, const void* s,
+                  int n_out, int m_rows, int k_in, int groupsize, int dev, int sms,
+                  cudaStream_t stream, int* status, const void* bias, int act, int meta_bits) {
+  const TcPlan pl = plan_decode_tc(n_out, k_in, sms, dev);
+  const int nr = (m_rows + 15) / 16 * 16;
+  const uint64_t N = n_out, K = k_in;
+  DecodeTcParams p;
+  const uint64_t a_dims[3] = {64, static_cast<uint64_t>(m_rows), K / 64};
+  const uint64_t a_strides[2] = {2 * K, 128};
+  const uint32_t a_box[3] = {64, static_cast<uint32_t>(nr), 4};
+  int rc = encode_nd(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, 3, a_dims, a_strides, a_box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 8,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  if (meta_bits == 3)
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, 3 * N / 8, K / 32, 3 * N, 48, 8,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 8,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  const bool grouped = groupsize != -1;
+  if (grouped) {
+    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, 2,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  } else {
+    std::memset(&p.tm_s, 0, sizeof(p.tm_s));
+  }
+  p.s = static_cast<const uint8_t*>(s);
+  p.C = static_cast<half*>(C);
+  p.bias = static_cast<const half*>(bias);
+  p.act = act;
+  p.status = status;
+  p.M = m_rows;
+  p.N = n_out;
+  p.ksteps = k_in / 256;
+  p.split = pl.split;
+  p.bpc = pl.bpc;
+  p.nblocks = n_out / 128;
+  p.pdl = pdl_enabled() ? 1 : 0;
+  p.trace = g_trace_buffer ? g_trace_buffer + g_trace_launch++ * kTraceLaunchWords : nullptr;
+  const int grid = pl.clusters * pl.split;
+  const bool m3 = meta_bits == 3;
+  switch (nr) {
+    case 16: return m3 ? dispatch_decode_tc<16, true>(p, grid, dev, stream, grouped)
+                       : dispatch_decode_tc<16, false>(p, grid, dev, stream, grouped);
+    case 32: return m3 ? dispatch_decode_tc<32, true>(p, grid, dev, stream, grouped)
+                       : dispatch_decode_tc<32, false>(p, grid, dev, stream, grouped);
+    case 48: return m3 ? dispatch_decode_tc<48, true>(p, grid, dev, stream, grouped)
+                       : dispatch_decode_tc<48, false>(p, grid, dev, stream, grouped);
+    case 64: return m3 ? dispatch_decode_tc<64, true>(p, grid, dev, stream, grouped)
+                       : dispatch_decode_tc<64, false>(p, grid, dev, stream, grouped);
+    default: return SM100_MARLIN_ERR_KERN_SHAPE;
+  }
+}
+
 // Fused all-gather targets of one call (see sm100_marlin_mul_2_4_gather).
 struct GatherArgs {
   int world, rank;
@@ -698,6 +814,18 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   if (sms <= 0) return SM100_MARLIN_ERR_ARGUMENT;
 
   if (gather && prob_n > 64) return SM100_MARLIN_ERR_ARGUMENT;
+  // Batches of 17 (3-bit metadata: 33) to 64 rows: the tensor-memory decode
+  // kernel, unless the call brings its own split-K scratch (_ex, _noalloc:
+  // the stream-K kernel below), gathers across GPUs, runs a metadata
+  // diagnostic, or has N not a multiple of 128 or K not a multiple of 256.
+  if (prob_n <= 64 && decode_tc_rows(prob_n, meta_bits) && !gather && scratch == nullptr &&
+      diag == 0 && prob_m % 128 == 0 && prob_k % 256 == 0) {
+    int* status = nullptr;
+    rc = device_status_ptr(dev, &status);
+    if (rc != SM100_MARLIN_OK) return rc;
+    return mul_decode_tc(A, B, meta, C, s, prob_m, prob_n, prob_k, groupsize, dev, sms, stream,
+                         status, bias, act, meta_bits);
+  }
   // The tcgen05 prefill kernels take batches above 64 rows, and 33-64 rows
   // where the CTA-pair kernel's tiles fit one wave and K <= 8192: there the
   // mma.sync decode kernel (4 row blocks) is compute-bound (Llama-7B at
@@ -1003,6 +1131,13 @@ int sm100_marlin_ipc_close(void* ptr, int dev) {
 
 int sm100_marlin_set_overlap(int enable) {
   g_pdl_override = enable ? 1 : 0;
+  return SM100_MARLIN_OK;
+}
+
+int sm100_marlin_set_decode_kernel(int which) {
+  if (which < SM100_MARLIN_DECODE_AUTO || which > SM100_MARLIN_DECODE_TMEM)
+    return SM100_MARLIN_ERR_ARGUMENT;
+  g_decode_kernel = which;
   return SM100_MARLIN_OK;
 }
 

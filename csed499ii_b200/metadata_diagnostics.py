@@ -14,7 +14,11 @@ the metadata path cut:
 
 Results are only meaningful when every metadata nibble is 0xE (int16 -4370,
 the reference's ``get_problem_24`` metadata); then they equal ``mul_2_4`` bit
-for bit (``kernel_profile/run.py:62-70``).  Group-128 scales only.
+for bit (``kernel_profile/run.py:62-70``) as long as ``mul_2_4`` runs the same
+kernel: the diagnostics are instances of the warp-level decode kernel and the
+CTA-pair kernel, so for 17-64 rows, which ``mul_2_4`` sends to the
+tensor-memory decode kernel by default, compare against a call made after
+``sm100_marlin_set_decode_kernel(DECODE_STREAM_K)``.  Group-128 scales only.
 """
 from __future__ import annotations
 

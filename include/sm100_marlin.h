@@ -248,6 +248,21 @@ const char* sm100_marlin_last_cuda_error(void);
  * counterpart in the reference (whose launches never overlap). */
 int sm100_marlin_set_overlap(int enable);
 
+/* Which kernel takes batches of at most 64 rows (process-wide):
+ *   SM100_MARLIN_DECODE_AUTO (0, default): the tensor-memory kernel for 17-64
+ *     rows (33-64 with 3-bit metadata) where N % 128 == 0 and K % 256 == 0,
+ *     the warp-level stream-K kernel otherwise;
+ *   SM100_MARLIN_DECODE_STREAM_K (1): always the warp-level kernel (or the
+ *     CTA-pair kernel for 33-64 rows where it applies);
+ *   SM100_MARLIN_DECODE_TMEM (2): the tensor-memory kernel for every batch of
+ *     1-64 rows whose shape it takes.
+ * Results of the two kernels agree within fp32 summation order; each is
+ * deterministic.  Returns SM100_MARLIN_ERR_ARGUMENT for other values. */
+#define SM100_MARLIN_DECODE_AUTO 0
+#define SM100_MARLIN_DECODE_STREAM_K 1
+#define SM100_MARLIN_DECODE_TMEM 2
+int sm100_marlin_set_decode_kernel(int which);
+
 /* Debug timelines: in a library built with -DSM100_MARLIN_TRACE=1 the k-th
  * GEMM launch after this call writes into `buf` (device memory, zeroed by the
  * caller, 36 KiB per launch) at offset k * 36 KiB: per CTA 16 uint64 words

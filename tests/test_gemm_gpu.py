@@ -285,23 +285,6 @@ def test_prefill_pair(K, N, M, g):
     check(run(A, B, meta, s, N, sms=8), oracle_c(A, W))
 
 
-# One CTA per 128-feature tile (tcgen05.mma.sp.cta_group::1): the launcher
-# uses it when N is not a multiple of 256 (pairs need 256 features).  128- and
-# 256-row batch tiles (a small `sms` selects 256), ragged batches, both scale
-# modes.
-@pytest.mark.parametrize("K,N,M,g,sms", [(1024, 640, 300, 128, -1), (512, 384, 200, -1, -1),
-                                         (2048, 1152, 1000, 128, 8), (1024, 1408, 257, -1, 8)])
-def test_prefill_single_cta(K, N, M, g, sms):
-    if g == -1:
-        W, B, s, meta = quantized_problem(N, K, -1, seed=K + N)
-    else:
-        W, B, s, meta = random_packed_problem(N, K, 128, seed=K + N + M)
-    A = activations(M, K, seed=M + 2)
-    C = run(A, B, meta, s, N, sms=sms)
-    check(C, oracle_c(A, W))
-    assert torch.equal(run(A, B, meta, s, N, sms=sms), C)
-
-
 def test_prefill_pair_deterministic():
     W, B, s, meta = random_packed_problem(2048, 1024, 128, seed=14)
     A = activations(384, 1024, seed=15)

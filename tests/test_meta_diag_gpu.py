@@ -8,7 +8,10 @@ whose metadata is the uniform pattern 0xEEEE
 (``kernel_experiments/sparse_marlin/kernel_profile/run.py:44-70``: random
 packed INT4 weights, scales 0.01, metadata -4370).  The same check here, on
 the decode kernel (1-16 rows and the 32-row tile), the CTA-pair route for
-33-64 rows and the CTA-pair prefill kernel.
+33-64 rows and the CTA-pair prefill kernel.  The diagnostics are instances
+of those kernels, so the baseline call pins them
+(``sm100_marlin_set_decode_kernel(DECODE_STREAM_K)``; by default 17-64 rows
+run on the tensor-memory decode kernel, whose sums come in another order).
 """
 import pytest
 import torch
@@ -32,13 +35,19 @@ def _uniform_problem(M, N, K, seed):
                                    (512, 4096, 4096), (200, 2048, 1024)])
 def test_diagnostics_equal_baseline_on_uniform_metadata(M, N, K):
     import csed499ii_b200 as m
+    from csed499ii_b200 import _ext
     from csed499ii_b200 import metadata_diagnostics as diag
 
     A, B, meta, s = _uniform_problem(M, N, K, seed=M + N)
     ws = torch.zeros(N // 128 * 16, dtype=torch.int32, device=DEV)
     C0 = torch.empty((M, N), dtype=torch.half, device=DEV)
-    m.mul_2_4(A, B, meta, C0, s, ws)
-    torch.cuda.synchronize()
+    lib = _ext.load()
+    assert lib.sm100_marlin_set_decode_kernel(_ext.DECODE_STREAM_K) == 0
+    try:
+        m.mul_2_4(A, B, meta, C0, s, ws)
+        torch.cuda.synchronize()
+    finally:
+        lib.sm100_marlin_set_decode_kernel(_ext.DECODE_AUTO)
     assert torch.isfinite(C0).all()
     for name in ("no_gmem", "no_reg", "no_all"):
         C = torch.full((M, N), float("nan"), dtype=torch.half, device=DEV)
