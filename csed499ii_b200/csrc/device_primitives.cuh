@@ -317,6 +317,13 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Arrive without waiting (the producer side of a named barrier whose other
+// participants bar.sync): memory accesses before the arrival are performed
+// for the waiting threads.
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Shared-memory loads
 // ---------------------------------------------------------------------------

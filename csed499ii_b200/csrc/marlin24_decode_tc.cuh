@@ -87,7 +87,17 @@ struct DecodeTcParams {
 // block's slot), 6 epilogue stored C, 8-14 inside the MMA warp's step (loop
 // top, tensor stage ready, activations ready, after the fence, after the
 // first and the last MMA, after the commits); word 1024 the CTA's clock at
-// entry.
+// entry, then setup stamps: 1025 barriers initialised (thread 0), 1026 tensor
+// memory allocated, 1027 past the CTA barrier, 1028 TMA warp 0 past the
+// programmatic-launch wait, 1029 epilogue past the cluster wait, 1030
+// epilogue past the programmatic-launch wait; in the dequantising warps word
+// 7 = first half stored to tensor memory, 15 = stores complete.
+// Every CTA c also records %globaltimer (ns, comparable across SMs) at words
+// kTcCtaBase + 8c + i: 0 entry, 1 first dequantisation start, 2 TMA warp
+// past the programmatic-launch wait, 3 first activations landed (MMA warp
+// 0), 4 last MMA issued, 5 last block's accumulators read, 6 last C stores
+// issued, 7 exit.
+constexpr int kTcCtaBase = 1088;
 constexpr int kTcTraceStages = 64;
 constexpr int kTcTraceWords = 16;
 
@@ -111,35 +121,56 @@ struct DecodeTcCfg {
   static constexpr int RECV = 128 * NR * 4;            // one exchange buffer
   static constexpr int OFF_RECV = HEADER;
   static constexpr int OFF_RING = HEADER + 2 * RECV;
-  // Both rings have an even depth: the two TMA warps, the two dequantising
-  // groups and the two MMA warps take stages by parity, so each then owns a
-  // fixed half of the slots and waits on a slot only after it waited on the
-  // slot's previous use (a barrier waited on by phase parity must never be
-  // two phases behind its waiter).
+  // MMA-issuing warps: a thread issues one tcgen05.mma per ~90-160 cycles
+  // whatever N is, and separate warps issue in parallel, so the 16-row tile
+  // (the least work per MMA) gets four, one per SM sub-partition.
+  static constexpr int MMA_WARPS = NR == 16 ? 4 : 2;
+  // Dequantising groups of four warps (one per tensor-memory lane quarter).
+  // The dequantisation is latency-bound (a warp issues ~0.25 instructions
+  // per cycle), so the 16-row tile, whose stages carry the least MMA work,
+  // runs four groups.
+  static constexpr int DG = NR == 16 ? 4 : 2;
+  // Ring depths are multiples of every role's warp count (two TMA warps, DG
+  // dequantising groups, MMA_WARPS MMA warps): each role takes stages in
+  // turn, so each warp (group) then owns a fixed subset of the slots and
+  // waits on a slot only after it waited on the slot's previous use (a
+  // barrier waited on by phase parity must never be two phases behind its
+  // waiter).
   static constexpr int DS_FIT = (SMEM_BUDGET - OFF_RING - 1024) / STAGE;
-  static constexpr int DS = (DS_FIT > 12 ? 12 : DS_FIT) & ~1;  // shared-memory stages
+  static constexpr int RING_MULT = MMA_WARPS > DG ? MMA_WARPS : DG;  // both powers of two
+  static constexpr int DS = (DS_FIT > 12 ? 12 : DS_FIT) / RING_MULT * RING_MULT;  // shared-memory stages
   static constexpr int SMEM = OFF_RING + DS * STAGE + 1024;
   // tensor memory: per stage 8 MMAs x (8 A + 4 metadata) columns; two
-  // accumulators (consecutive blocks) for each of the two MMA-issuing warps
+  // accumulators (consecutive blocks) for each MMA-issuing warp
   static constexpr int TSLOT = KS * 48;
-  static constexpr int MMA_WARPS = 2;
   static constexpr int ACC_COLS = MMA_WARPS * 2 * NR;
   static constexpr int DT_FIT = (TMEM_COLS - ACC_COLS) / TSLOT;
-  static constexpr int DT = (DT_FIT > 4 ? 4 : DT_FIT) & ~1;    // tensor-memory stages
-  // warps: 0-1 TMA, 2-3 MMA, then DG groups of four dequantising warps, then
-  // four epilogue warps
-  static constexpr int DG = 2;
+  static constexpr int DT = (DT_FIT > 4 ? 4 : DT_FIT) / RING_MULT * RING_MULT;  // tensor-memory stages
+  // warps: 0-1 TMA, MMA_WARPS MMA, then DG groups of four dequantising warps,
+  // then four epilogue warps
   static constexpr int WARP_MMA = 2;
-  static constexpr int WARP_DQ = 4;
+  static constexpr int WARP_DQ = WARP_MMA + MMA_WARPS;
   static constexpr int WARP_EPI = WARP_DQ + 4 * DG;
   static constexpr int THREADS = (WARP_EPI + 4) * 32;
-  static_assert(DS >= 2 && DT >= 2 && DS % 2 == 0 && DT % 2 == 0, "ring depths");
-  static_assert((3 * DS + 2 * DT + 8) * 8 <= 1000, "barriers exceed the header");
+  static_assert(DS >= RING_MULT && DT >= RING_MULT && DS % RING_MULT == 0 &&
+                    DT % RING_MULT == 0 && DS % 2 == 0,
+                "ring depths");
+  static constexpr int NBAR = 3 * DS + 2 * DT + 8;
+  static_assert(NBAR * 8 <= 1000, "barriers exceed the header");
 };
 
 // Row m = 32q + l of a block holds feature 32q + phi(l) (see the file comment).
 __device__ __forceinline__ int tc_row_feature(int l) {
   return 8 * ((l & 7) >> 1) + 2 * (l & 1) + (l >> 4) + 4 * ((l >> 3) & 1);
+}
+
+__device__ __forceinline__ void tmem_st32_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_st32_x32(uint32_t taddr, const uint32_t (&v)[32]) {
@@ -247,6 +278,12 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   unsigned long long* const trace = (SM100_MARLIN_TRACE && p.trace && blockIdx.x == 0) ? p.trace : nullptr;
+  unsigned long long* const cta_trace =
+      (SM100_MARLIN_TRACE && p.trace) ? p.trace + kTcCtaBase + 8 * blockIdx.x : nullptr;
+  auto gstamp = [&](int i) {
+    if (cta_trace) cta_trace[i] = global_timer_ns();
+  };
+  if (threadIdx.x == 0) gstamp(0);
   if (trace && threadIdx.x == 0) trace[kTcTraceWords * kTcTraceStages] = clock64();
   auto stamp = [&](int s, int i) {
     if (trace && lane == 0 && s < kTcTraceStages) trace[kTcTraceWords * s + i] = clock64();
@@ -258,43 +295,58 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
   const int k_lo = static_cast<int>(rank) * p.ksteps / S;
   const int kn = (static_cast<int>(rank) + 1) * p.ksteps / S - k_lo;  // stages per block (>= 1)
   const int T = nb * kn;                                              // stages of this CTA
-  // MMA warp w takes the stages s with s % 2 == w (with one stage per block,
-  // warp 0 takes them all: every block's accumulator then has one writer)
-  const int mma_warps = kn >= 2 ? 2 : 1;
+  // MMA warp w takes the stages s with s % mma_warps == w; mma_warps (1, 2 or
+  // 4, a divisor of both ring depths) is at most the stages per block, so
+  // every active MMA warp writes every block's accumulator
+  const int mma_warps = kn >= Cfg::MMA_WARPS ? Cfg::MMA_WARPS : (kn >= 2 ? 2 : 1);
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < DS; ++i) {
-      mbar_init(smem_addr(&sfull[i]), 1);
-      mbar_init(smem_addr(&afull[i]), 1);
-      mbar_init(smem_addr(&sempty[i]), 5);
+  if (warp == 0) {
+    // the barriers are contiguous from sfull: lane i initialises i, i + 32, ...
+    for (int i = lane; i < Cfg::NBAR; i += 32) {
+      uint32_t count = 1;  // sfull, afull, tempty, recvb
+      if (i >= 2 * DS && i < 3 * DS) count = 5;  // sempty
+      else if (i >= 3 * DS && i < 3 * DS + DT) count = 4;  // tready
+      else if (i >= 3 * DS + 2 * DT && i < 3 * DS + 2 * DT + 2) count = mma_warps;  // accfull
+      else if (i >= 3 * DS + 2 * DT + 2 && i < 3 * DS + 2 * DT + 4) count = 4;  // accempty
+      else if (i >= 3 * DS + 2 * DT + 6) count = S;  // freeb
+      mbar_init(smem_addr(&sfull[i]), count);
     }
-    for (int i = 0; i < DT; ++i) {
-      mbar_init(smem_addr(&tready[i]), 4);
-      mbar_init(smem_addr(&tempty[i]), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_addr(&accfull[i]), mma_warps);
-      mbar_init(smem_addr(&accempty[i]), 4);
-      mbar_init(smem_addr(&recvb[i]), 1);
-      mbar_init(smem_addr(&freeb[i]), S);
-    }
-    *abort_flag = 0;
     fence_mbar_init();
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
     prefetch_tmap(&p.tm_act);
     prefetch_tmap(&p.tm_b);
     prefetch_tmap(&p.tm_meta);
     if (GROUPED) prefetch_tmap(&p.tm_s);
+    if (trace) trace[kTcTraceWords * kTcTraceStages + 1] = clock64();
   }
-  if (warp == Cfg::WARP_MMA) tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
+  if (warp == Cfg::WARP_MMA) {
+    tmem_alloc(smem_addr(tmem_slot), Cfg::TMEM_COLS);
+    if (trace && lane == 0) trace[kTcTraceWords * kTcTraceStages + 2] = clock64();
+  }
   // let the next kernel on the stream start streaming its weights
   if (p.pdl && threadIdx.x == 0) grid_dependency_launch();
-  tc_fence_before();
-  if (S > 1)
-    cluster_sync_all();  // peers' barriers exist before any remote arrive or st.async
-  else
-    __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  // Start-up.  The TMA warps need only the barriers, which warp 0 has
+  // initialised: they pass named barrier 2 together and start streaming.
+  // The other warps also need the tensor-memory address: they wait on named
+  // barrier 3, where warps 0-1 only arrive.
+  uint32_t tmem = 0;
+  if (warp < Cfg::WARP_MMA) {
+    named_bar_sync(2, 64);
+    named_bar_arrive(3, Cfg::THREADS);
+  } else {
+    tc_fence_before();
+    named_bar_sync(3, Cfg::THREADS);
+    tc_fence_after();
+    tmem = *tmem_slot;
+  }
+  if (trace && threadIdx.x == 0) trace[kTcTraceWords * kTcTraceStages + 3] = clock64();
+  // The weight stream needs only this CTA's barriers; the cluster barrier
+  // (peers' barriers exist before any remote arrive or st.async) is waited
+  // on by the epilogue warps before their first exchange, and by the others
+  // at teardown.
+  if (S > 1) cluster_arrive_relaxed();  // after the barrier-init fences
   const uint32_t ring = smem_addr(smem + Cfg::OFF_RING);
 
   if (warp < Cfg::WARP_MMA) {
@@ -327,6 +379,8 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
         if (!waited) {  // a stage frees only after its MMAs, which need the activations
           grid_dependency_wait();
           waited = true;
+          if (trace && threadIdx.x == 0) trace[kTcTraceWords * kTcTraceStages + 4] = clock64();
+          if (threadIdx.x == 0) gstamp(2);
           if (lane == 0)
             for (int i = 0; i < n_pend; ++i) issue_act(pend_slot[i], pend_ks[i]);
           n_pend = 0;
@@ -363,15 +417,17 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
     }
     if (!waited) {
       grid_dependency_wait();
+      if (trace && threadIdx.x == 0) trace[kTcTraceWords * kTcTraceStages + 4] = clock64();
+      if (threadIdx.x == 0) gstamp(2);
       if (lane == 0)
         for (int i = 0; i < n_pend; ++i) issue_act(pend_slot[i], pend_ks[i]);
     }
   } else if (warp < Cfg::WARP_DQ) {
     // ------------------------------------------------------------- MMA issue
-    // Two warps, one thread each, take the stages in turn, each accumulating
-    // into its own accumulator: one warp's barrier waits and commits (100-200
-    // cycles each) overlap the other's MMAs.  The epilogue adds the two
-    // accumulators in a fixed order.
+    // MMA_WARPS warps, one thread each, take the stages in turn, each
+    // accumulating into its own accumulator: the warps' MMA issue, barrier
+    // waits and commits (100-200 cycles each) overlap.  The epilogue adds the
+    // accumulators in warp order.
     const int w = warp - Cfg::WARP_MMA;
     constexpr uint32_t idesc = umma_idesc_f16_f32(NR) | (1u << 2);  // sparse
     constexpr uint64_t kAtom = (NR * 128) >> 4;                     // next 64-K atom
@@ -380,7 +436,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
       uint32_t sph = 0, tph = 0;  // phase parities of slot / t
       bool first = true;          // this warp's first stage of block j
       for (int s = 0; s < T; ++s) {
-        if ((s & 1) == w || mma_warps == 1) {
+        if ((s & (mma_warps - 1)) == w) {
           bool ok = true;
           stamp(s, 8);
           if (first && j >= 2)  // the epilogue has read this accumulator out
@@ -389,6 +445,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
           stamp(s, 9);
           ok = ok && mbar_wait_spin_sleep_bounded(smem_addr(&afull[slot]), sph, abort_flag);
           stamp(s, 10);
+          if (s == 0 && lane == 0) gstamp(3);
           if (!__all_sync(0xffffffffu, ok)) {
             if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
             break;
@@ -404,6 +461,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
               umma_sp_f16_ts(acc, ta + 8 * i, bd + (i >> 1) * kAtom + (i & 1) * 4,
                              ta + 32 * KS + 4 * i, idesc, (first && i == 0) ? 0u : 1u);
             stamp(s, 13);
+            if (s + mma_warps >= T) gstamp(4);
             umma_commit(smem_addr(&tempty[t]));
             umma_commit(smem_addr(&sempty[slot]));
             // this warp's last stage of the block
@@ -457,68 +515,76 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
       }
       tc_fence_after();
       if (q == 0) stamp(s, 1);
+      if (s == 0 && q == 0 && lane == 0) gstamp(1);
       const uint8_t* stp = smem + Cfg::OFF_RING + slot * Cfg::STAGE;
       const uint32_t tslot = lane_base + t * Cfg::TSLOT;
+      // four sub-steps of 64 K (two 32-K rows each; a small register
+      // footprint leaves room for four dequantising groups)
 #pragma unroll
-      for (int h = 0; h < KS; ++h) {
+      for (int u = 0; u < 2 * KS; ++u) {
+        const int h = u >> 1;        // 128-K half of the stage
+        const int kb = 2 * (u & 1);  // first 32-K row of the sub-step in the half
         // plain loads (ordered after the barrier wait by its memory clobber),
         // all issued before any use so that their latencies overlap
-        uint32_t words[16];
+        uint32_t words[8];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
+        for (int k2 = 0; k2 < 2; ++k2)
 #pragma unroll
           for (int tt = 0; tt < 4; ++tt)
-            words[kk * 4 + tt] = *reinterpret_cast<const uint32_t*>(
-                stp + code_off + (4 * h + kk) * 1024 + 16 * tt);
-        uint32_t mraw[META3 ? 8 : 4];
+            words[k2 * 4 + tt] = *reinterpret_cast<const uint32_t*>(
+                stp + code_off + (4 * h + kb + k2) * 1024 + 16 * tt);
+        uint32_t mraw[META3 ? 4 : 2];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          mraw[kk] = *reinterpret_cast<const uint32_t*>(stp + meta_off + (4 * h + kk) * Cfg::META_ROW);
-          if constexpr (META3)
-            mraw[4 + kk] = *reinterpret_cast<const uint32_t*>(stp + meta_off + (4 * h + kk) * Cfg::META_ROW + 64);
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const uint8_t* mp = stp + meta_off + (4 * h + kb + k2) * Cfg::META_ROW;
+          mraw[k2] = *reinterpret_cast<const uint32_t*>(mp);
+          if constexpr (META3) mraw[2 + k2] = *reinterpret_cast<const uint32_t*>(mp + 64);
         }
         half2 s2 = __float2half2_rn(1.f);
         if (GROUPED) {
           const half sh = *reinterpret_cast<const half*>(stp + scale_off + 256 * h);
           s2 = __halves2half2(sh, sh);
         }
-        uint32_t v[32];
+        uint32_t v[16];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int k2 = 0; k2 < 2; ++k2) {
 #pragma unroll
           for (int tt = 0; tt < 4; ++tt) {
-            const uint32_t wd = words[kk * 4 + tt];
+            const uint32_t wd = words[k2 * 4 + tt];
             half2 lo, hi;
             dequant_pair_sched(e ? (wd >> 8) : wd, lo, hi);  // (kc 2tt, 2tt+1), (kc 8+2tt, 9+2tt)
             if (GROUPED) {
               lo = __hmul2(lo, s2);
               hi = __hmul2(hi, s2);
             }
-            v[kk * 8 + tt] = *reinterpret_cast<uint32_t*>(&lo);
-            v[kk * 8 + 4 + tt] = *reinterpret_cast<uint32_t*>(&hi);
+            v[k2 * 8 + tt] = *reinterpret_cast<uint32_t*>(&lo);
+            v[k2 * 8 + 4 + tt] = *reinterpret_cast<uint32_t*>(&hi);
           }
         }
-        uint32_t mw[4];
+        uint32_t mw[2];
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int k2 = 0; k2 < 2; ++k2) {
           if constexpr (META3) {
             // 4-bit word w4 of the chunk is the high (w4 < 32) or low decode of
             // 3-bit words w4 % 32 and w4 % 32 + 16 (meta3_pair_decode)
-            const uint32_t a = mraw[kk], bb = mraw[4 + kk];
+            const uint32_t a = mraw[k2], bb = mraw[2 + k2];
             const bool upper = (w4 & 31) >= 16;
             if (w4 >= 32)
-              mw[kk] = decode24_low(upper ? (bb >> 8) : __funnelshift_r(a, bb, 24));
+              mw[k2] = decode24_low(upper ? (bb >> 8) : __funnelshift_r(a, bb, 24));
             else
-              mw[kk] = decode24_high(upper ? __funnelshift_r(a, bb, 16) : a);
+              mw[k2] = decode24_high(upper ? __funnelshift_r(a, bb, 16) : a);
           } else {
-            mw[kk] = mraw[kk];
+            mw[k2] = mraw[k2];
           }
         }
-        tmem_st32_x32(tslot + 32 * h, v);
+        tmem_st32_x16(tslot + 32 * h + 8 * kb, v);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tmem_st32(tslot + 32 * KS + 16 * h + 4 * kk, mw[kk]);
+        for (int k2 = 0; k2 < 2; ++k2)
+          tmem_st32(tslot + 32 * KS + 16 * h + 4 * (kb + k2), mw[k2]);
+        if (q == 0 && u == 1) stamp(s, 7);
       }
       tmem_wait_st();
+      if (q == 0) stamp(s, 15);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -539,15 +605,19 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
     const uint32_t lane_acc = tmem + (static_cast<uint32_t>(32 * q) << 16);
     // C may still be read by the previous kernel on the stream
     if (p.pdl) grid_dependency_wait();
+    if (trace && et == 0) trace[kTcTraceWords * kTcTraceStages + 6] = clock64();
+    if (S > 1) cluster_wait();
+    if (trace && et == 0) trace[kTcTraceWords * kTcTraceStages + 5] = clock64();
     for (int j = 0; j < nb; ++j) {
       const int buf = j & 1;
-      bool ok = mbar_wait_sleep_bounded(smem_addr(&accfull[buf]), (j >> 1) & 1, abort_flag);
+      bool ok = mbar_wait_spin_sleep_bounded(smem_addr(&accfull[buf]), (j >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
         break;
       }
       tc_fence_after();
       if (q == 0) stamp(j * kn, 5);
+      if (j == nb - 1 && et == 0) gstamp(5);
       // sum of the MMA warps' accumulators, warp 0 first
       uint32_t r[NR];
       float acc[NR];
@@ -556,9 +626,9 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
       tmem_wait_ld();
 #pragma unroll
       for (int u = 0; u < NR; ++u) acc[u] = __uint_as_float(r[u]);
-      if (mma_warps == 2) {
+      for (int w = 1; w < mma_warps; ++w) {
 #pragma unroll
-        for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + (2 + buf) * NR + c0, r + c0);
+        for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + (2 * w + buf) * NR + c0, r + c0);
         tmem_wait_ld();
 #pragma unroll
         for (int u = 0; u < NR; ++u) acc[u] += __uint_as_float(r[u]);
@@ -583,8 +653,10 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
 #pragma unroll
         for (int c0 = 0; c0 < NR; c0 += 4)
           st_async_v4(rdst + 4 * c0, make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]), rbar);
+        if (q == 0) stamp(j * kn, 11);
         if (et == 0) mbar_arrive_expect_tx(smem_addr(&recvb[buf]), Cfg::RECV);
-        ok = mbar_wait_sleep_bounded(smem_addr(&recvb[buf]), (j >> 1) & 1, abort_flag);
+        ok = mbar_wait_spin_sleep_bounded(smem_addr(&recvb[buf]), (j >> 1) & 1, abort_flag);
+        if (q == 0) stamp(j * kn, 12);
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
           break;
@@ -642,6 +714,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
       }
       named_bar_sync(1, 128);
       if (q == 0) stamp(j * kn, 6);
+      if (j == nb - 1 && et == 0) gstamp(6);
       // release buffer `buf` to every CTA of the cluster (needed only when a
       // block j + 2 follows)
       if (S > 1 && j + 2 < nb && et < S)
@@ -649,20 +722,22 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
     }
   }
 
-  // Teardown: all MMAs complete before the tensor memory is released, and no
-  // CTA of the cluster leaves while a peer may still write to its shared
-  // memory.
+  // Teardown: all MMAs complete before the tensor memory is released.  No
+  // cluster barrier: every remote write aimed at a CTA (its peers' st.async
+  // partials, counted on its recvb, and their freeb arrivals, which it waits
+  // for before its exchange of block j + 2) precedes a wait that the CTA has
+  // passed by the end of its last exchange, so a CTA may leave as soon as it
+  // is done.  Each thread completes its start-up cluster arrival.
+  if (S > 1 && warp < Cfg::WARP_EPI) cluster_wait();
   tc_fence_before();
   __syncthreads();
-  if (warp == Cfg::WARP_MMA && *abort_flag == 0)  // the last block's accumulators are complete
-    mbar_wait_sleep_bounded(smem_addr(&accfull[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort_flag);
-  tc_fence_before();
-  if (S > 1)
-    cluster_sync_all();
-  else
-    __syncthreads();
-  tc_fence_after();
-  if (warp == Cfg::WARP_MMA) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  if (warp == Cfg::WARP_MMA) {
+    if (*abort_flag == 0)  // the last block's accumulators are complete
+      mbar_wait_sleep_bounded(smem_addr(&accfull[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort_flag);
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) gstamp(7);
 }
 
 }  // namespace sm100

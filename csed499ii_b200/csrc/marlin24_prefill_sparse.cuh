@@ -405,6 +405,18 @@ __device__ __forceinline__ void cluster_sync_all() {
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of a cluster barrier, for a CTA whose threads arrive early
+// and wait later (each thread waits once per arrival, in order).  The
+// relaxed arrival orders nothing by itself: mbarrier initialisations are
+// published to the cluster by fence.mbarrier_init.release.cluster first.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
