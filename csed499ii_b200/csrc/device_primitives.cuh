@@ -311,6 +311,50 @@ __device__ __forceinline__ void grid_dependency_wait() {
 }
 
 // ---------------------------------------------------------------------------
+// Thread-block clusters: rank, distributed shared memory, cluster barrier.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The two halves of a cluster barrier, for a CTA whose threads arrive early
+// and wait later (each thread waits once per arrival, in order).  The
+// relaxed arrival orders nothing by itself: mbarrier initialisations are
+// published to the cluster by fence.mbarrier_init.release.cluster first.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16 bytes into another CTA's shared memory (shared::cluster address), the
+// bytes counted on that CTA's mbarrier (shared::cluster address).
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, const float4& v, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          cluster_addr),
+      "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+      "r"(__float_as_uint(v.w)), "r"(cluster_bar)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Named barriers for subsets of warps (id 0 is __syncthreads).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {

@@ -210,17 +210,6 @@ __device__ __forceinline__ void umma_sp_f16_ts(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
-// 16 bytes into another CTA's shared memory (shared::cluster address), the
-// bytes counted on that CTA's mbarrier (shared::cluster address).
-__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, const float4& v, uint32_t cluster_bar) {
-  asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-          cluster_addr),
-      "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
-      "r"(__float_as_uint(v.w)), "r"(cluster_bar)
-      : "memory");
-}
-
 __device__ __forceinline__ void sts128(uint32_t addr, const float4& v) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
                "f"(v.w)

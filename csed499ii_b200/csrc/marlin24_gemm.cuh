@@ -33,6 +33,9 @@
 //    publish their partials and count them without waiting, a producer thread
 //    of the finisher polls the counter while its consumers still compute, and
 //    the finisher adds the partials in CTA order (deterministic) and writes C.
+//    When the tiles times 2 or 3 fill the SMs, the CTAs of a tile form one
+//    thread-block cluster instead and send their partials into the
+//    finisher's shared memory with st.async (cluster split-K, no scratch).
 #pragma once
 
 #include <cuda.h>
@@ -81,6 +84,12 @@ struct GemmParams {
   int gather_world;                                  // 0: plain stores to C
   int gather_rank;
   int tiles_per_rank;                                // tiles each rank stores per call
+  // Cluster split-K (batch <= 16): 0 or 1 for the stream-K split over the
+  // whole grid; S = 2 or 3 when the grid is n_tiles * S CTAs launched as
+  // clusters of S, one cluster per column tile.  The CTAs of a tile then
+  // hand their partials to the tile's finisher (cluster rank 0) through
+  // distributed shared memory instead of the scratch and counters.
+  int cluster;
 };
 
 // Per-CTA timeline written when the library is built with
@@ -228,6 +237,8 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int S = p.cluster > 1 ? p.cluster : 1;
+  const uint32_t crank = S > 1 ? cluster_cta_rank() : 0u;
   unsigned long long* trace =
       SM100_MARLIN_TRACE && p.trace ? p.trace + static_cast<long long>(blockIdx.x) * kTraceWords : nullptr;
   if (trace && threadIdx.x == 0) {
@@ -244,6 +255,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     *abort_flag = 0;
     mbar_init(smem_addr(fin_bar), 1);
     fence_mbar_init();
+    // cluster split-K: rank 0 finishes the tile and receives the S - 1
+    // partials of the other ranks, counted as bytes on fin_bar
+    if (S > 1 && crank == 0)
+      mbar_arrive_expect_tx(smem_addr(fin_bar), static_cast<uint32_t>((S - 1) * NC * Cfg::ACC_BYTES));
   }
   if constexpr ((DIAG & kDiagNoGmem) != 0) {
     // uniform metadata in every stage's region, written once (never copied)
@@ -263,6 +278,10 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     if (GROUPED) prefetch_tmap(&p.tm_s);
   }
   __syncthreads();
+  // the peers' barriers exist before any st.async (waited on by each warp
+  // before its first remote store, or before it leaves)
+  if (S > 1) cluster_arrive_relaxed();
+  bool cluster_waited = false;
 
   const long long grid = gridDim.x;
   const long long cta = blockIdx.x;
@@ -350,7 +369,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       // their partials to be published, then hand over to the consumers.
       // The counters are only read after griddepcontrol.wait (above), so the
       // previous kernel's use of them is over.
-      if (pw == 0 && ok) {
+      if (pw == 0 && ok && S == 1) {
         const long long last_tile = (u_end - 1) / units_per_tile;
         const long long t0 = last_tile * units_per_tile;
         if (u_begin <= t0 && u_end < t0 + units_per_tile) {
@@ -378,6 +397,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         }
       }
     }
+    if (S > 1) cluster_wait();
     return;
   }
 
@@ -619,6 +639,22 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
 
     if (trace && threadIdx.x == 0) trace[8] = global_timer_ns();
     const bool complete = (kb == 0 && ke == p.kk_total);
+    if (!complete && kb != 0 && S > 1) {
+      // 2a') cluster contributor (rank r > 0): the leader warp of each chunk
+      //      stores its partial into slot r - 1 of the finisher's (rank 0)
+      //      partial buffer, the bytes counted on the finisher's fin_bar.
+      //      Nothing aims at this CTA afterwards, so it may leave at once.
+      if (wk == 0) {
+        cluster_wait();
+        cluster_waited = true;
+        const uint32_t dst = mapa_shared(
+            smem_addr(fin) + (((crank - 1) * NC + cc) * Cfg::ACC_F4 * 32 + lane) * 16, 0);
+        const uint32_t rbar = mapa_shared(smem_addr(fin_bar), 0);
+#pragma unroll
+        for (int v = 0; v < Cfg::ACC_F4; ++v) st_async_v4(dst + v * 512, acc4[v], rbar);
+      }
+      continue;
+    }
     if (!complete && kb != 0) {
       // 2a) contributor: this segment ends a tile that another CTA (the one
       //     holding the tile's first K units) finishes.  Publish the partial
@@ -689,7 +725,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         }
       }
       // every contribution has arrived and been counted: re-arm the counter
-      if (cc == 0 && lane == 0) p.counters[tile] = 0;
+      if (cc == 0 && lane == 0 && S == 1) p.counters[tile] = 0;
     }
     // 3) the leader warp of each chunk converts and stores 16-byte rows of C.
     if (threadIdx.x == 0) ++tiles_stored;
@@ -790,6 +826,7 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
       }
     }
   }
+  if (S > 1 && !cluster_waited) cluster_wait();
   if (trace && threadIdx.x == 0) trace[4] = global_timer_ns();
 }
 

@@ -387,36 +387,6 @@ struct PrefillSp2Cfg {
   static_assert((3 * DEPTH + 1) * 8 <= HEADER - 8, "barriers exceed the header");
 };
 
-__device__ __forceinline__ uint32_t cluster_cta_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// shared::cluster address of the same shared-memory offset in CTA `rank`
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The two halves of a cluster barrier, for a CTA whose threads arrive early
-// and wait later (each thread waits once per arrival, in order).  The
-// relaxed arrival orders nothing by itself: mbarrier initialisations are
-// published to the cluster by fence.mbarrier_init.release.cluster first.
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 __device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");

@@ -21,9 +21,10 @@ from problems import REL_FRO_TOL, REL_MAE_TOL, activations, errors, random_packe
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
-# Llama-2-7B qkv and down projections: at 1 and 16 batch rows the plan splits
-# K across CTAs (more CTAs than column tiles).
-SPLIT_K_CASES = [(12288, 4096, 1), (4096, 11008, 16), (12288, 4096, 16), (4096, 11008, 1)]
+# Llama-2-7B gate+up and Llama-2-70B qkv projections: at 1 and 16 batch rows
+# the plan splits K across CTAs through the scratch (stream-K: more column
+# tiles than CTAs, and too many for a cluster per tile).
+SPLIT_K_CASES = [(22016, 4096, 1), (10240, 8192, 16), (22016, 4096, 16), (10240, 8192, 1)]
 
 
 def _call(fn, A, B, meta, C, s, ws, N, M, K):
