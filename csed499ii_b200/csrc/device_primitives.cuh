@@ -465,11 +465,14 @@ __device__ __forceinline__ void mma_sp_16832_z(float (&d)[4], const uint32_t (&a
 // 3-bit metadata decode.
 //
 // Eight 3-bit codes in bits [0,24) are spread to nibbles (code i in bits
-// [4i, 4i+3)), then every output bit is one lop3 over the three code bits
-// aligned to that position.  LUT byte bit v = output bit for code v; the two
-// tables are the codec's "high" map [E,D,8,D,3,4,9,C] and "low" map
+// [4i, 4i+3), bit 3 of every nibble clear), and each nibble then selects one
+// byte of an 8-entry table with prmt (codes 0-3 from the first table word,
+// 4-7 from the second); two prmts give the eight looked-up values as bytes,
+// which are merged pairwise into nibbles and gathered by a third prmt.  The
+// two tables are the codec's "high" map [E,D,8,D,3,4,9,C] and "low" map
 // [C,D,E,A,8,9,4,0] (codes 3/4 resp. 3/7 are never produced by the packer).
-// Bits [24,32) of the input are ignored.
+// Bits [24,32) of the input are ignored.  15 instructions per word (the
+// earlier form, one lop3 per output bit position, took ~23).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t spread24(uint32_t x) {
   constexpr int kSel = ((0xAA & 0xF0) | (~0xAA & 0xCC)) & 0xFF;  // c ? a : b (bitwise)
@@ -479,22 +482,29 @@ __device__ __forceinline__ uint32_t spread24(uint32_t x) {
   return x;
 }
 
-template <int L0, int L1, int L2, int L3>
-__device__ __forceinline__ uint32_t decode_spread(uint32_t x) {
-  // lop3 argument order (a, b, c) = (code bit 2, code bit 1, code bit 0).
-  const uint32_t b0 = lop3<L0>(x >> 2, x >> 1, x) & 0x11111111u;
-  const uint32_t b1 = lop3<L1>(x >> 1, x, x << 1) & 0x22222222u;
-  const uint32_t b2 = lop3<L2>(x, x << 1, x << 2) & 0x44444444u;
-  const uint32_t b3 = lop3<L3>(x << 1, x << 2, x << 3) & 0x88888888u;
-  return (b0 | b1) | (b2 | b3);
+__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+template <uint32_t LUT_LO, uint32_t LUT_HI>
+__device__ __forceinline__ uint32_t decode24_lut(uint32_t x) {
+  // bit 3 of each nibble would switch prmt to sign replication: keep it clear
+  const uint32_t sel = spread24(x) & 0x77777777u;
+  uint32_t r0 = prmt_b32(LUT_LO, LUT_HI, sel);        // bytes: values of codes 0-3
+  uint32_t r1 = prmt_b32(LUT_LO, LUT_HI, sel >> 16);  // codes 4-7
+  r0 |= r0 >> 4;  // byte 0 = v0 | v1 << 4, byte 2 = v2 | v3 << 4
+  r1 |= r1 >> 4;
+  return prmt_b32(r0, r1, 0x6420u);
 }
 
 __device__ __forceinline__ uint32_t decode24_high(uint32_t x) {
-  return decode_spread<0x5A, 0x11, 0xAB, 0xCF>(spread24(x));
+  return decode24_lut<0x0D080D0Eu, 0x0C090403u>(x);  // [E,D,8,D | 3,4,9,C]
 }
 
 __device__ __forceinline__ uint32_t decode24_low(uint32_t x) {
-  return decode_spread<0x22, 0x0C, 0x47, 0x3F>(spread24(x));
+  return decode24_lut<0x0A0E0D0Cu, 0x00040908u>(x);  // [C,D,E,A | 8,9,4,0]
 }
 
 // Lane-pair decode: lanes 0..15 hold (X, Y) words of their 48-bit pair,
