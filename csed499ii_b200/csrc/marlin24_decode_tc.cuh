@@ -72,7 +72,7 @@ struct DecodeTcParams {
   int* status;          // device status word
   int M;
   int N;
-  int ksteps;           // K / 256 (stages per block)
+  int ksteps;           // K / (128 * tc_stage_ks(NR)) (stages per block)
   int split;            // S: CTAs of a cluster splitting K (1, 2 or 4)
   int bpc;              // 128-feature blocks per cluster
   int nblocks;          // N / 128
@@ -101,10 +101,15 @@ constexpr int kTcCtaBase = 1088;
 constexpr int kTcTraceStages = 64;
 constexpr int kTcTraceWords = 16;
 
+// 128-K sub-steps per stage: 2 (256-K stages), or 1 for the 48- and 64-row
+// tiles, whose activation slice (24 or 32 KB per 256 K) would otherwise leave
+// room for only two stages.
+__host__ __device__ constexpr int tc_stage_ks(int nr) { return nr >= 48 ? 1 : 2; }
+
 template <int NR, bool META3>
 struct DecodeTcCfg {
   static_assert(NR == 16 || NR == 32 || NR == 48 || NR == 64, "batch tile");
-  static constexpr int KS = 2;                         // 128-K sub-steps per stage (256 K)
+  static constexpr int KS = tc_stage_ks(NR);           // 128-K sub-steps per stage
   static constexpr int SMEM_BUDGET = 227 * 1024;       // one CTA per SM
   static constexpr int TMEM_COLS = 512;
   static constexpr int ACT = 2 * KS * NR * 128;        // 64-K atoms of NR rows
@@ -145,7 +150,8 @@ struct DecodeTcCfg {
   static constexpr int TSLOT = KS * 48;
   static constexpr int ACC_COLS = MMA_WARPS * 2 * NR;
   static constexpr int DT_FIT = (TMEM_COLS - ACC_COLS) / TSLOT;
-  static constexpr int DT = (DT_FIT > 4 ? 4 : DT_FIT) / RING_MULT * RING_MULT;  // tensor-memory stages
+  static constexpr int DT_CAP = 4 * 2 / KS;  // at most 1024 K in tensor memory
+  static constexpr int DT = (DT_FIT > DT_CAP ? DT_CAP : DT_FIT) / RING_MULT * RING_MULT;  // tensor-memory stages
   // warps: 0-1 TMA, MMA_WARPS MMA, then DG groups of four dequantising warps,
   // then four epilogue warps
   static constexpr int WARP_MMA = 2;

@@ -737,8 +737,8 @@ struct TcPlan {
   int split, bpc, clusters;
 };
 
-TcPlan plan_decode_tc(int n_out, int k_in, int sms, int dev) {
-  const int nblocks = n_out / 128, ksteps = k_in / 256;  // 256-K stages
+TcPlan plan_decode_tc(int n_out, int k_in, int kstage, int sms, int dev) {
+  const int nblocks = n_out / 128, ksteps = k_in / kstage;  // stages of kstage K
   TcPlan best{1, nblocks, 1};
   long long best_cost = -1;
   for (int split : {1, 2, 4}) {
@@ -765,33 +765,35 @@ int dispatch_decode_tc(const DecodeTcParams& p, int grid, int dev, cudaStream_t 
 }
 
 // C[M, N] = A . dequant(B, meta, s) for M <= 64, N % 128 == 0, K % 256 == 0
-// on the tensor-memory decode kernel (stages of 256 K: 8 rows of 32 K).
+// on the tensor-memory decode kernel (stages of 256 K, or 128 K for tiles of
+// 48 and 64 rows: tc_stage_ks).
 int mul_decode_tc(const void* A, const void* B, const void* meta, void* C, const void* s,
                   int n_out, int m_rows, int k_in, int groupsize, int dev, int sms,
                   cudaStream_t stream, int* status, const void* bias, int act, int meta_bits) {
-  const TcPlan pl = plan_decode_tc(n_out, k_in, sms, dev);
   const int nr = (m_rows + 15) / 16 * 16;
+  const int ks = tc_stage_ks(nr);  // 128-K sub-steps per stage
+  const TcPlan pl = plan_decode_tc(n_out, k_in, 128 * ks, sms, dev);
   const uint64_t N = n_out, K = k_in;
   DecodeTcParams p;
   const uint64_t a_dims[3] = {64, static_cast<uint64_t>(m_rows), K / 64};
   const uint64_t a_strides[2] = {2 * K, 128};
-  const uint32_t a_box[3] = {64, static_cast<uint32_t>(nr), 4};
+  const uint32_t a_box[3] = {64, static_cast<uint32_t>(nr), static_cast<uint32_t>(2 * ks)};
   int rc = encode_nd(&p.tm_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, A, 3, a_dims, a_strides, a_box,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 8,
+  rc = encode_2d(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT64, B, N, K / 32, 8 * N, 128, 4 * ks,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   if (meta_bits == 3)
-    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, 3 * N / 8, K / 32, 3 * N, 48, 8,
-                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, 3 * N / 8, K / 32, 3 * N, 48,
+                   4 * ks, CU_TENSOR_MAP_SWIZZLE_NONE);
   else
-    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64, 8,
-                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    rc = encode_2d(&p.tm_meta, CU_TENSOR_MAP_DATA_TYPE_UINT64, meta, N / 2, K / 32, 4 * N, 64,
+                   4 * ks, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   const bool grouped = groupsize != -1;
   if (grouped) {
-    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, 2,
+    rc = encode_2d(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_UINT64, s, N / 4, K / 128, 2 * N, 32, ks,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   } else {
@@ -804,7 +806,7 @@ int mul_decode_tc(const void* A, const void* B, const void* meta, void* C, const
   p.status = status;
   p.M = m_rows;
   p.N = n_out;
-  p.ksteps = k_in / 256;
+  p.ksteps = k_in / (128 * ks);
   p.split = pl.split;
   p.bpc = pl.bpc;
   p.nblocks = n_out / 128;
