@@ -168,10 +168,14 @@ def bench_ours(args, torch, dist, rank, world, dev):
     fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
     stream = torch.cuda.Stream(device=dev)
     # N > 1, default: the all-gather fused into the GEMM epilogue (peer stores
-    # over NVLink into buffers shared by CUDA IPC); --gather nccl: separate
-    # NCCL all-gather after each GEMM
-    fused = world > 1 and args.gather == "fused"
-    fg = shard.FusedGather(M, max(N for _, N in SHAPES), device=dev) if fused else None
+    # over NVLink into buffers shared by CUDA IPC), pipelined: each GEMM's
+    # kernel ends once the previous call's exchange has completed, and every
+    # step ends with a wait for its last exchange (so each step's all-gathers
+    # are complete inside the timed region); --gather nccl: separate NCCL
+    # all-gather after each GEMM
+    fused = world > 1 and args.gather in ("fused", "fused-sync")
+    fg = (shard.FusedGather(M, max(N for _, N in SHAPES), device=dev,
+                            pipelined=args.gather == "fused") if fused else None)
     shards = [[shard.ShardedWeight.from_local(B, meta, s, rank * N, (rank + 1) * N, args.meta_bits)
                for (K, N), (B, meta, s) in zip(SHAPES, lay)] for lay in layers] if fused else None
 
@@ -179,12 +183,9 @@ def bench_ours(args, torch, dist, rank, world, dev):
         for li, lay in enumerate(layers):
             for si, ((K, N), (B, meta, s)) in enumerate(zip(SHAPES, lay)):
                 if fused:
-                    b = fg.next
-                    fg.next ^= 1
-                    rc = lib.sm100_marlin_mul_2_4_gather(
-                        A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(), N, M, K,
-                        shards[li][si].workspace.data_ptr(), GROUP // 2, devi, s_ptr,
-                        args.meta_bits, fg._c[b], fg._flag[b], fg._seen[b], world, rank)
+                    rc, _ = fg.issue(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(),
+                                     N, M, K, shards[li][si].workspace.data_ptr(), GROUP // 2,
+                                     s_ptr, args.meta_bits)
                 else:
                     rc = fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(),
                             s.data_ptr(), N, M, K, ws.data_ptr(), GROUP // 2, devi, s_ptr, -1, -1,
@@ -193,6 +194,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
                     raise RuntimeError(f"mul_2_4 failed: {m._ext.describe(rc)}")
                 if not fused:
                     gather(N)
+        if fused:
+            fg.wait(s_ptr)
 
     bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
     launches_step = args.layers * len(SHAPES) * ((M + 63) // 64)
@@ -243,16 +246,14 @@ def bench_ours(args, torch, dist, rank, world, dev):
             for li, lay in enumerate(layers):
                 B, meta, s = lay[idx]
                 if fused:
-                    b = fg.next
-                    fg.next ^= 1
-                    lib.sm100_marlin_mul_2_4_gather(
-                        A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(), N, M, K,
-                        shards[li][idx].workspace.data_ptr(), GROUP // 2, devi, sp,
-                        args.meta_bits, fg._c[b], fg._flag[b], fg._seen[b], world, rank)
+                    fg.issue(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(), N, M, K,
+                             shards[li][idx].workspace.data_ptr(), GROUP // 2, sp, args.meta_bits)
                 else:
                     fn(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), C[N].data_ptr(),
                        s.data_ptr(), N, M, K, ws.data_ptr(), GROUP // 2, devi, sp, -1, -1, -1, 16)
                     gather(N)
+            if fused:
+                fg.wait(sp)
         for _ in range(3):
             g2.replay()
         torch.cuda.synchronize(dev)
@@ -289,6 +290,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
                 else:
                     md.matmul(A_d[K], B, meta, C[N], s, ws)
                 gather(N)
+        if fused:
+            fg.wait()
         for N in C_h:
             C_h[N].copy_(C_out[N], non_blocking=True)
 
@@ -674,9 +677,11 @@ def main():
     ap.add_argument("--m", type=int, default=16)
     ap.add_argument("--meta-bits", type=int, choices=[3, 4], default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+    ap.add_argument("--gather", choices=["fused", "fused-sync", "nccl"], default="fused",
                     help="N > 1: all-gather of C fused into the GEMM epilogue (NVLink peer "
-                         "stores) or a separate NCCL all-gather")
+                         "stores) with pipelined completion (each step ends with a wait for "
+                         "its last exchange), the same with per-call completion, or a "
+                         "separate NCCL all-gather")
     ap.add_argument("--workload", choices=["decode", "prefill", "ablation"], default="decode",
                     help="decode: Llama-2-7B decode step (config 1, the headline); "
                          "prefill: compute-bound sweep (config 4); ablation: metadata-cost "

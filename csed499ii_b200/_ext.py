@@ -50,8 +50,9 @@ SIGNATURES = {
     "sm100_marlin_pack_2_4": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                                        _vp]),
     "sm100_marlin_mul_2_4_gather": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp,
-                                             _c_int, _c_int, _vp, _c_int, _vp, _vp, _vp, _c_int,
-                                             _c_int]),
+                                             _c_int, _c_int, _vp, _c_int, _vp, _vp, _vp, _vp, _vp,
+                                             _vp, _c_int, _c_int, _c_int]),
+    "sm100_marlin_gather_wait": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _vp]),
     "sm100_marlin_ipc_alloc": (_c_int, [_size, _c_int, ctypes.POINTER(_vp)]),
     "sm100_marlin_ipc_free": (_c_int, [_vp, _c_int]),
     "sm100_marlin_ipc_get_handle": (_c_int, [_vp, _c_int, _vp]),

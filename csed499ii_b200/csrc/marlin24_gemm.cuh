@@ -75,11 +75,25 @@ struct GemmParams {
   // Fused all-gather of column-parallel shards (gather_world > 0): every C row
   // this launch computes is stored into each rank's gathered buffer (peer
   // memory over NVLink) at this rank's column block, then counted on each
-  // rank's arrival counter; CTA 0 returns only once its own counter shows the
-  // blocks of every rank for this call.
+  // rank's arrival counter:
+  //  - per-call release (gather_defer = 0): each CTA, after its stores, with a
+  //    system-scope fence and the number of tiles it stored;
+  //  - deferred release (gather_defer = 1): no CTA waits for its stores; a
+  //    later launch (the next call's CTA 0, right after its programmatic-
+  //    launch wait, through gather_release; or the completion wait) fences
+  //    once, when this launch has completed, and adds 1 per rank.
+  // CTA 0 adds this call's count (world x tiles_per_rank, or world) to the
+  // buffer's cumulative target, then returns only once the counter
+  // gather_wait_arrival has reached *gather_wait_target: this call's own
+  // counter and target (the call completes with its all-gather), an earlier
+  // call's (pipelined completion), or nothing (null).
   half* gather_c[kMaxGatherRanks];                   // each rank's gathered C (row 0 of this launch)
   unsigned long long* gather_flag[kMaxGatherRanks];  // each rank's arrival counter
-  unsigned long long* gather_seen;                   // arrivals this rank has already waited for
+  unsigned long long* gather_target;                 // this rank's cumulative target of this buffer
+  const unsigned long long* gather_wait_arrival;     // counter this launch waits on, or null
+  const unsigned long long* gather_wait_target;      // the target it waits for
+  unsigned long long* gather_release[kMaxGatherRanks];  // previous call's counters (deferred), or null
+  int gather_defer;                                  // 1: deferred release of this call
   long long gather_ldc;                              // row stride of the gathered C (elements)
   int gather_world;                                  // 0: plain stores to C
   int gather_rank;
@@ -313,9 +327,21 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
         tma_load_3d(ring_base + slot * Cfg::STAGE + Cfg::OFF_A, &p.tm_a, 0, 0, kk0 >> 1, full,
                     pol_keep);
       };
+      // Deferred all-gather release of the previous call (CTA 0): once the
+      // previous launch has completed (programmatic-launch wait, or a launch
+      // without overlap), its peer stores are done; one system-scope fence
+      // orders them before the counts.
+      auto release_previous_gather = [&]() {
+        if (blockIdx.x == 0 && pw == 0 && p.gather_release[0] != nullptr) {
+          fence_acq_rel_sys();
+          for (int q = 0; q < p.gather_world; ++q) red_add_relaxed_sys_u64(p.gather_release[q], 1ull);
+        }
+      };
+      if (waited) release_previous_gather();
       auto release_deferred = [&]() {
         grid_dependency_wait();
         waited = true;
+        release_previous_gather();
         for (int i = 0; i < n_pre; ++i) issue_a(pre_slot[i], pre_kk[i]);
         n_pre = 0;
       };
@@ -793,36 +819,36 @@ __global__ void __launch_bounds__(DecodeCfg<NC, MB, META3>::THREADS, 1)
     // every consumer warp's C stores precede thread 0's system-scope release
     named_bar_sync(1, kConsumerWarps * 32);
     if (threadIdx.x == 0) {
-      if (tiles_stored > 0) {
+      if (!p.gather_defer && tiles_stored > 0) {
         fence_acq_rel_sys();
         for (int q = 0; q < p.gather_world; ++q)
           red_add_relaxed_sys_u64(p.gather_flag[q], static_cast<unsigned long long>(tiles_stored));
       }
       if (blockIdx.x == 0) {
-        // the launch completes only when this rank holds every rank's block:
-        // the arrival counter only grows; `seen` (device memory, so graph
-        // replays advance it too) is where the previous call's wait ended
-        const unsigned long long seen = *p.gather_seen;
-        const unsigned long long target =
-            seen + static_cast<unsigned long long>(p.gather_world) * p.tiles_per_rank;
-        const unsigned long long* own = p.gather_flag[p.gather_rank];
-        unsigned long long t0 = 0;
-        uint32_t polls = 0;
-        while (ld_acquire_sys_u64(own) < target) {
-          if ((++polls & 63u) != 0) continue;
-          const unsigned long long now = global_timer_ns();
-          if (t0 == 0) {
-            t0 = now;
-          } else if (now - t0 > kWaitLimitNs) {
-            atomicOr(p.status, kStatusGatherWaitTimeout);
-            break;
+        // Arrival counters and targets only grow (device memory, so graph
+        // replays advance them too).  The target moves by this call's blocks
+        // whether or not a wait below expires: late arrivals still count
+        // toward this call, so a later wait on the buffer is for later calls'
+        // blocks, not for this call's stragglers.  The buffer's previous
+        // target was written by an earlier launch, visible since this thread
+        // passed the programmatic-launch wait in its epilogue.
+        *p.gather_target += static_cast<unsigned long long>(p.gather_world) *
+                            (p.gather_defer ? 1ull : static_cast<unsigned long long>(p.tiles_per_rank));
+        if (p.gather_wait_arrival != nullptr) {
+          const unsigned long long want = *p.gather_wait_target;
+          unsigned long long t0 = 0;
+          uint32_t polls = 0;
+          while (ld_acquire_sys_u64(p.gather_wait_arrival) < want) {
+            if ((++polls & 63u) != 0) continue;
+            const unsigned long long now = global_timer_ns();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
+              atomicOr(p.status, kStatusGatherWaitTimeout);  // the waited-for output is incomplete
+              break;
+            }
           }
         }
-        // Advanced on expiry too: arrivals that come late still count toward
-        // this call's target, so the next call on the buffer waits for its own
-        // blocks rather than for this call's stragglers.  The status bit tells
-        // the host that this call's output is incomplete.
-        *p.gather_seen = target;
       }
     }
   }

@@ -832,7 +832,11 @@ struct GatherArgs {
   int world, rank;
   void* const* c;
   void* const* flag;
-  void* seen;
+  void* target;
+  const void* wait_arrival;
+  const void* wait_target;
+  void* const* release;  // previous call's counters (deferred release), or null
+  int defer;
 };
 
 int mul_impl(const void* A, const void* B, const void* meta, void* C, const void* s, int prob_m,
@@ -898,7 +902,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
   }
 
   const int chunk_rows = prob_n < 64 ? prob_n : 64;
-  Plan big = make_plan(prob_m, chunk_rows, prob_k, sms, gather == nullptr);
+  Plan big = make_plan(prob_m, chunk_rows, prob_k, sms);
   if (scratch == nullptr) {
     rc = get_scratch(dev, stream, big.scratch, &scratch);
     if (rc != SM100_MARLIN_OK) return rc;
@@ -911,7 +915,7 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
 
   for (int r0 = 0; r0 < prob_n; r0 += 64) {
     const int rows = (prob_n - r0) < 64 ? (prob_n - r0) : 64;
-    Plan pl = make_plan(prob_m, rows, prob_k, sms, gather == nullptr);
+    Plan pl = make_plan(prob_m, rows, prob_k, sms);
     GemmParams p;
     const uint8_t* a_rows = static_cast<const uint8_t*>(A) + static_cast<size_t>(r0) * prob_k * 2;
     p.s = static_cast<const uint8_t*>(s);
@@ -934,22 +938,30 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     p.act = act;
     p.gather_world = 0;
     p.gather_rank = 0;
-    p.gather_seen = nullptr;
+    p.gather_target = nullptr;
+    p.gather_wait_arrival = nullptr;
+    p.gather_wait_target = nullptr;
     p.gather_ldc = 0;
     p.tiles_per_rank = 0;
+    p.gather_defer = 0;
     for (int q = 0; q < kMaxGatherRanks; ++q) {
       p.gather_c[q] = nullptr;
       p.gather_flag[q] = nullptr;
+      p.gather_release[q] = nullptr;
     }
     if (gather) {
       p.gather_world = gather->world;
       p.gather_rank = gather->rank;
-      p.gather_seen = static_cast<unsigned long long*>(gather->seen);
+      p.gather_target = static_cast<unsigned long long*>(gather->target);
+      p.gather_wait_arrival = static_cast<const unsigned long long*>(gather->wait_arrival);
+      p.gather_wait_target = static_cast<const unsigned long long*>(gather->wait_target);
       p.gather_ldc = static_cast<long long>(gather->world) * prob_m;
       p.tiles_per_rank = prob_m / (64 * pl.nc);
+      p.gather_defer = gather->defer;
       for (int q = 0; q < gather->world; ++q) {
         p.gather_c[q] = static_cast<half*>(gather->c[q]);
         p.gather_flag[q] = static_cast<unsigned long long*>(gather->flag[q]);
+        if (gather->release) p.gather_release[q] = static_cast<unsigned long long*>(gather->release[q]);
       }
       p.C = p.gather_c[gather->rank];
     }
@@ -960,6 +972,46 @@ int mul_impl(const void* A, const void* B, const void* meta, void* C, const void
     if (rc != SM100_MARLIN_OK) return rc;
   }
   return SM100_MARLIN_OK;
+}
+
+}  // namespace
+}  // namespace sm100
+
+namespace sm100 {
+namespace {
+
+struct GatherWaitParams {
+  const unsigned long long* arrival;
+  const unsigned long long* target;
+  unsigned long long* release[kMaxGatherRanks];  // deferred release to do first, or null
+  int world;
+  int* status;
+};
+
+// One thread: the deferred release of the last fused all-gather call (when
+// given; the previous launch on the stream has completed, so its peer stores
+// are done), then a bounded wait until this rank's arrival counter of a
+// buffer reaches the buffer's target (sm100_marlin_gather_wait).
+__global__ void gather_wait_kernel(const __grid_constant__ GatherWaitParams p) {
+  if (p.release[0] != nullptr) {
+    fence_acq_rel_sys();
+    for (int q = 0; q < p.world; ++q) red_add_relaxed_sys_u64(p.release[q], 1ull);
+  }
+  const unsigned long long* arrival = p.arrival;
+  int* status = p.status;
+  const unsigned long long want = *p.target;
+  unsigned long long t0 = 0;
+  uint32_t polls = 0;
+  while (ld_acquire_sys_u64(arrival) < want) {
+    if ((++polls & 63u) != 0) continue;
+    const unsigned long long now = global_timer_ns();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
+      atomicOr(status, kStatusGatherWaitTimeout);
+      break;
+    }
+  }
 }
 
 }  // namespace
@@ -1119,18 +1171,53 @@ int sm100_marlin_pack_2_4(const void* w, const void* s, int prob_k, int prob_m, 
 int sm100_marlin_mul_2_4_gather(const void* A, const void* B, const void* meta, const void* s,
                                 int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
                                 int dev, void* stream, int meta_bits, void* const* gathered_c,
-                                void* const* arrival, void* seen, int world, int rank) {
+                                void* const* arrival, void* target, const void* wait_arrival,
+                                const void* wait_target, void* const* release_arrival, int defer,
+                                int world, int rank) {
   if (world < 1 || world > kMaxGatherRanks || rank < 0 || rank >= world) return SM100_MARLIN_ERR_ARGUMENT;
   if (meta_bits != 3 && meta_bits != 4) return SM100_MARLIN_ERR_ARGUMENT;
-  if (!gathered_c || !arrival || !seen) return SM100_MARLIN_ERR_ARGUMENT;
+  if (!gathered_c || !arrival || !target || (wait_arrival == nullptr) != (wait_target == nullptr))
+    return SM100_MARLIN_ERR_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(target) & 7u) || (reinterpret_cast<uintptr_t>(wait_arrival) & 7u) ||
+      (reinterpret_cast<uintptr_t>(wait_target) & 7u))
+    return SM100_MARLIN_ERR_ALIGNMENT;
+  if (defer != 0 && defer != 1) return SM100_MARLIN_ERR_ARGUMENT;
   for (int q = 0; q < world; ++q) {
     if (!gathered_c[q] || !arrival[q] || (reinterpret_cast<uintptr_t>(gathered_c[q]) & 15u) ||
         (reinterpret_cast<uintptr_t>(arrival[q]) & 7u))
       return SM100_MARLIN_ERR_ALIGNMENT;
+    if (release_arrival &&
+        (!release_arrival[q] || (reinterpret_cast<uintptr_t>(release_arrival[q]) & 7u)))
+      return SM100_MARLIN_ERR_ALIGNMENT;
   }
-  const GatherArgs g{world, rank, gathered_c, arrival, seen};
+  const GatherArgs g{world,       rank,        gathered_c,      arrival, target,
+                     wait_arrival, wait_target, release_arrival, defer};
   return mul_impl(A, B, meta, gathered_c[rank], s, prob_m, prob_n, prob_k, workspace, groupsize,
                   dev, stream, -1, -1, -1, 16, meta_bits, nullptr, 0, &g);
+}
+
+int sm100_marlin_gather_wait(const void* arrival, const void* target, void* const* release_arrival,
+                             int world, int dev, void* stream) {
+  if (!arrival || !target) return SM100_MARLIN_ERR_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(arrival) & 7u) || (reinterpret_cast<uintptr_t>(target) & 7u))
+    return SM100_MARLIN_ERR_ALIGNMENT;
+  if (release_arrival && (world < 1 || world > kMaxGatherRanks)) return SM100_MARLIN_ERR_ARGUMENT;
+  GatherWaitParams wp{};
+  wp.arrival = static_cast<const unsigned long long*>(arrival);
+  wp.target = static_cast<const unsigned long long*>(target);
+  wp.world = release_arrival ? world : 0;
+  for (int q = 0; q < wp.world; ++q) {
+    if (!release_arrival[q] || (reinterpret_cast<uintptr_t>(release_arrival[q]) & 7u))
+      return SM100_MARLIN_ERR_ALIGNMENT;
+    wp.release[q] = static_cast<unsigned long long*>(release_arrival[q]);
+  }
+  DeviceGuard guard(dev);
+  if (!guard.ok) return cuda_fail(cudaGetLastError());
+  int rc = device_status_ptr(dev, &wp.status);
+  if (rc != SM100_MARLIN_OK) return rc;
+  gather_wait_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(wp);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SM100_MARLIN_OK : cuda_fail(e);
 }
 
 int sm100_marlin_ipc_alloc(size_t bytes, int dev, void** ptr) {

@@ -130,17 +130,31 @@ class _DevArray:
 class FusedGather:
     """Output buffers for the GEMM with the all-gather fused into its epilogue.
 
-    Every rank of ``group`` allocates one device region (CUDA IPC) holding two
-    gathered outputs of up to ``max_rows x (world * max_cols)`` fp16 and, per
-    buffer, an arrival counter and a "seen" word; the regions are exported,
-    exchanged with ``all_gather_object`` and mapped into every rank.  Calls
-    alternate between the two buffers, so a rank that already stores the next
-    call's block never overwrites one another rank may still be reading (the
-    fused call completes only when its own buffer holds all blocks).  All
-    ranks must make the same sequence of calls.
+    Every rank of ``group`` allocates one device region (CUDA IPC) holding
+    three gathered outputs of up to ``max_rows x (world * max_cols)`` fp16
+    and, per buffer, an arrival counter and a cumulative target; the regions
+    are exported, exchanged with ``all_gather_object`` and mapped into every
+    rank.  Calls rotate over the buffers.  All ranks must make the same
+    sequence of calls.
+
+    Completion (``pipelined``):
+
+    * ``False``: each call completes on the stream only once this rank's
+      buffer holds every rank's block (two buffers in turn suffice: a rank can
+      be at most one call ahead).
+    * ``True`` (default): no CTA waits for its own peer stores; the next
+      call (or :meth:`wait`) releases them once this call's kernel has
+      completed, and each call's kernel ends once the PREVIOUS call's
+      exchange has completed, so a call's all-gather overlaps the next GEMM.
+      A call's output is complete after :meth:`wait` -- call it before
+      reading the output, and read it before the next call.  Three buffers
+      rotate, because a rank can then be one call further ahead.
     """
 
-    def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
+    BUFFERS = 3
+
+    def __init__(self, max_rows: int, max_cols: int, group=None, device=None,
+                 pipelined: bool = True):
         from . import _ext
 
         self._lib = _ext.load()
@@ -149,8 +163,10 @@ class FusedGather:
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dev = dev.index if dev.index is not None else torch.cuda.current_device()
         self.max_rows, self.max_cols = max_rows, max_cols
+        self.pipelined = pipelined
+        nb = self.BUFFERS
         self._c_bytes = (max_rows * self.world * max_cols * 2 + 255) // 256 * 256
-        total = 2 * self._c_bytes + 256
+        total = nb * self._c_bytes + 256
         base = ctypes.c_void_p()
         self._check(self._lib.sm100_marlin_ipc_alloc(total, self.dev, ctypes.byref(base)))
         self._own = base.value
@@ -170,18 +186,65 @@ class FusedGather:
                 self._check(self._lib.sm100_marlin_ipc_open(h, self.dev, ctypes.byref(peer)))
                 self._opened.append(peer.value)
                 bases.append(peer.value)
+        # region: nb gathered outputs, then per buffer i the arrival counter at
+        # +8i and this rank's cumulative target at +128 + 8i (all zero at start)
+        tail = nb * self._c_bytes
         self._c = [(ctypes.c_void_p * self.world)(*[b + i * self._c_bytes for b in bases])
-                   for i in range(2)]
-        self._flag = [(ctypes.c_void_p * self.world)(*[b + 2 * self._c_bytes + 8 * i for b in bases])
-                      for i in range(2)]
-        self._seen = [self._own + 2 * self._c_bytes + 128 + 8 * i for i in range(2)]
+                   for i in range(nb)]
+        self._flag = [(ctypes.c_void_p * self.world)(*[b + tail + 8 * i for b in bases])
+                      for i in range(nb)]
+        self._target = [self._own + tail + 128 + 8 * i for i in range(nb)]
         self.next = 0
+        self._last = None     # buffer of the last call (pipelined: its completion is pending)
+        self._unreleased = None  # buffer of a call whose deferred release is pending
 
     def _check(self, err):
         from . import _ext
 
         if err != _ext.OK:
             raise RuntimeError(f"fused all-gather setup failed: {_ext.describe(err)}")
+
+    def _wait_args(self, buf: int):
+        """(arrival, target) the launch for ``buf`` waits on before it ends."""
+        if not self.pipelined:
+            return self._flag[buf][self.rank], self._target[buf]
+        if self._last is None:
+            return None, None
+        return self._flag[self._last][self.rank], self._target[self._last]
+
+    def issue(self, a_ptr, b_ptr, meta_ptr, s_ptr, cols, m, k, workspace_ptr, groupsize,
+              stream_ptr, meta_bits):
+        """Launch the fused GEMM + all-gather on raw device pointers (the
+        operands of :func:`mul_2_4_gathered`) on ``stream_ptr``; returns the
+        library status and the buffer written."""
+        buf = self.next
+        self.next = (self.next + 1) % self.BUFFERS
+        wait_arrival, wait_target = self._wait_args(buf)
+        release = self._flag[self._unreleased] if self._unreleased is not None else None
+        err = self._lib.sm100_marlin_mul_2_4_gather(
+            a_ptr, b_ptr, meta_ptr, s_ptr, cols, m, k, workspace_ptr, groupsize, self.dev,
+            stream_ptr, meta_bits, self._c[buf], self._flag[buf], self._target[buf], wait_arrival,
+            wait_target, release, 1 if self.pipelined else 0, self.world, self.rank)
+        if err == 0:
+            self._last = buf
+            self._unreleased = buf if self.pipelined else None
+        return err, buf
+
+    def wait(self, stream_ptr=None) -> None:
+        """Make the last call's all-gather complete on the stream (default:
+        the current one).  Pipelined mode; a no-op otherwise, where every call
+        completes with its own exchange."""
+        from . import _ext, _stream_ptr
+
+        if not self.pipelined or self._last is None:
+            return
+        release = self._flag[self._unreleased] if self._unreleased is not None else None
+        err = self._lib.sm100_marlin_gather_wait(
+            self._flag[self._last][self.rank], self._target[self._last], release, self.world,
+            self.dev, _stream_ptr(self.dev) if stream_ptr is None else stream_ptr)
+        if err != _ext.OK:
+            raise RuntimeError(f"fused all-gather wait failed: {_ext.describe(err)}")
+        self._unreleased = None
 
     def output(self, buf: int, rows: int, cols: int) -> torch.Tensor:
         """This rank's gathered buffer ``buf`` as an ``(rows, world*cols)`` fp16 tensor."""
@@ -222,11 +285,15 @@ def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather,
                      check: bool = False):
     """``A @ W`` for the column-sharded W with the all-gather fused into the
     GEMM: returns this rank's ``(M, world * N/world)`` fp16 result (a view of
-    the fused buffer, valid until the call after next).
+    the fused buffer).
 
-    The call is asynchronous.  A rank whose peers do not arrive within the
-    kernel's wait limit gets an incomplete result and a device status bit;
-    ``check=True`` synchronises and raises in that case (otherwise call
+    The call is asynchronous.  With a pipelined ``gather`` (the default) the
+    result is complete after ``gather.wait()`` and must be read before the
+    next call on ``gather``; otherwise it is complete when the call completes
+    on the stream and stays valid until the call after next.  A rank whose
+    peers do not arrive within the kernel's wait limit gets an incomplete
+    result and a device status bit; ``check=True`` waits (pipelined),
+    synchronises and raises in that case (otherwise call
     :func:`check_status` at a synchronisation point of your own)."""
     from . import _ext, _groupsize, _stream_ptr
 
@@ -236,15 +303,15 @@ def mul_2_4_gathered(A: torch.Tensor, shard: ShardedWeight, gather: FusedGather,
         raise ValueError("fused all-gather: at most 64 (and max_rows) rows, max_cols columns")
     if not (A.is_cuda and A.dtype == torch.half and A.is_contiguous()):
         raise RuntimeError("A must be a contiguous CUDA half tensor")
-    buf = gather.next
-    gather.next ^= 1
     dev = A.get_device()
-    err = gather._lib.sm100_marlin_mul_2_4_gather(
-        A.data_ptr(), shard.B.data_ptr(), shard.meta.data_ptr(), shard.s.data_ptr(), cols, m, k,
-        shard.workspace.data_ptr(), _groupsize(k, shard.s), dev, _stream_ptr(dev), shard.meta_bits,
-        gather._c[buf], gather._flag[buf], gather._seen[buf], gather.world, gather.rank)
+    if dev != gather.dev:
+        raise ValueError("A must be on the FusedGather's device")
+    err, buf = gather.issue(A.data_ptr(), shard.B.data_ptr(), shard.meta.data_ptr(),
+                            shard.s.data_ptr(), cols, m, k, shard.workspace.data_ptr(),
+                            _groupsize(k, shard.s), _stream_ptr(dev), shard.meta_bits)
     if err != _ext.OK:
         raise RuntimeError(f"fused sharded GEMM failed: {_ext.describe(err)}")
     if check:
+        gather.wait()
         check_status(dev)
     return gather.output(buf, m, cols)

@@ -169,20 +169,51 @@ int sm100_marlin_mul_2_4_meta_diag(const void* A, const void* B, const void* met
  *                  row-major, mapped into this process (sm100_marlin_ipc_open)
  *   arrival[q]     rank q's uint64 arrival counter for that buffer (zero at
  *                  creation, never reset)
- *   seen           this rank's uint64: arrivals already waited for on the
- *                  buffer (zero at creation; advanced on the device)
+ *   target         this rank's uint64 cumulative target for that buffer (zero
+ *                  at creation; the call adds its blocks, world x tiles, on
+ *                  the device)
+ *   wait_arrival,  the launch ends once *wait_arrival >= *wait_target
+ *   wait_target    (bounded wait, SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT on
+ *                  expiry); both null: no wait
+ *   release_arrival  the previous call's arrival counters (all ranks) when
+ *                  that call deferred its release, else null
+ *   defer          0: every CTA releases its own stores (system-scope fence,
+ *                  then its tile count on every rank's counter); 1: this
+ *                  call's stores are released later, by the next call
+ *                  (release_arrival) or by sm100_marlin_gather_wait, which
+ *                  add 1 per rank once this launch has completed
  * Every C row this rank computes is stored into all ranks' gathered buffers
- * (peer stores over NVLink) at column block `rank`; the call completes on the
- * stream once this rank's buffer holds every rank's block (bounded wait,
- * SM100_MARLIN_STATUS_GATHER_WAIT_TIMEOUT on expiry).  All ranks must issue
- * the same sequence of calls on a buffer (shapes may differ between calls).  A rank may already store its next
- * call's block while another still reads this one, so alternate two buffers
- * between consecutive calls.
+ * (peer stores over NVLink) at column block `rank`.  Completion, chosen by the
+ * caller:
+ *   - per call (defer = 0, no release_arrival): wait_arrival =
+ *     arrival[rank], wait_target = target; the call completes on the stream
+ *     once this rank's buffer holds every rank's block.  A rank may already
+ *     store its next call's block while another still reads this one, so
+ *     alternate two buffers between calls.
+ *   - pipelined (defer = 1): release_arrival and the wait are the PREVIOUS
+ *     call's (its counters; its arrival[rank] and target), both null for the
+ *     first call, and a sequence ends with sm100_marlin_gather_wait on the
+ *     last call (releasing it).  A call's exchange then overlaps the next
+ *     GEMM and no CTA waits for its own peer stores; a call's output is
+ *     complete once a later launch waited on it.  Rotate three buffers (a
+ *     rank can be one call further ahead) and read a call's output before
+ *     issuing the next call.
+ * All ranks must issue the same sequence of calls on a buffer (shapes may
+ * differ between calls).
  */
 int sm100_marlin_mul_2_4_gather(const void* A, const void* B, const void* meta, const void* s,
                                 int prob_m, int prob_n, int prob_k, void* workspace, int groupsize,
                                 int dev, void* stream, int meta_bits, void* const* gathered_c,
-                                void* const* arrival, void* seen, int world, int rank);
+                                void* const* arrival, void* target, const void* wait_arrival,
+                                const void* wait_target, void* const* release_arrival, int defer,
+                                int world, int rank);
+
+/* On `stream` (one-thread kernel): the deferred release of the last call
+ * (release_arrival: its counters on all `world` ranks, or null), then a
+ * bounded wait until *arrival >= *target -- the completion point of a
+ * pipelined fused all-gather (see above).  No counterpart in the reference. */
+int sm100_marlin_gather_wait(const void* arrival, const void* target, void* const* release_arrival,
+                             int world, int dev, void* stream);
 
 /* Device buffers shared between processes (CUDA IPC) for the fused all-gather:
  * allocate (zeroed), export a 64-byte handle, map a peer's buffer, unmap,

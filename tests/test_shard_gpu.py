@@ -4,6 +4,9 @@
   placed in its column block; the assembled C must match the oracle.
 * Two GPUs (skipped with fewer): two NCCL ranks run ``mul_2_4_sharded`` (local
   GEMM + all-gather of C) and both must hold the oracle's C.
+* The all-gather fused into the GEMM (``mul_2_4_gathered``), with per-call and
+  with pipelined completion (``FusedGather.wait()`` before reading), on one
+  rank and on two GPUs.
 """
 import os
 import socket
@@ -89,12 +92,13 @@ def test_two_rank_nccl_all_gather():
         assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (rank, rel_mae, rel_fro)
 
 
-def test_fused_gather_one_rank():
+@pytest.mark.parametrize("pipelined", [True, False])
+def test_fused_gather_one_rank(pipelined):
     """The fused path with a single rank (its own buffer is the only peer):
-    alternating buffers, changing shapes, the device-side arrival accounting."""
+    rotating buffers, changing shapes, the device-side arrival accounting."""
     import csed499ii_b200 as m
 
-    gather = shard.FusedGather(64, 4096, device=DEV)
+    gather = shard.FusedGather(64, 4096, device=DEV, pipelined=pipelined)
     try:
         cases = [(4096, 4096, 16), (4096, 2048, 1), (1024, 4096, 64), (4096, 4096, 16),
                  (2048, 1024, 5)]
@@ -104,6 +108,7 @@ def test_fused_gather_one_rank():
                                      torch.from_numpy(s).to(DEV), 0, 1)
             A = torch.from_numpy(activations(M, K, seed=i)).to(DEV)
             C = shard.mul_2_4_gathered(A, sw, gather)
+            gather.wait()
             torch.cuda.synchronize()
             assert C.shape == (M, N)
             rel_mae, rel_fro, _ = errors(C, A.float() @ torch.from_numpy(W).to(DEV).float())
@@ -113,7 +118,33 @@ def test_fused_gather_one_rank():
         gather.close()
 
 
-def _fused_worker(rank, world, port, q):
+def test_fused_gather_pipelined_sequence():
+    """Pipelined completion over a sequence with no waits in between (each
+    launch waits on its predecessor's exchange): the last result, after one
+    wait, is complete; nothing timed out."""
+    import csed499ii_b200 as m
+
+    gather = shard.FusedGather(16, 4096, device=DEV)
+    try:
+        N, K, M = 4096, 4096, 16
+        outs = []
+        for i in range(7):
+            W, B, s, meta = random_packed_problem(N, K, 128, seed=300 + i)
+            sw = shard.ShardedWeight(torch.from_numpy(B).to(DEV), torch.from_numpy(meta).to(DEV),
+                                     torch.from_numpy(s).to(DEV), 0, 1)
+            A = torch.from_numpy(activations(M, K, seed=40 + i)).to(DEV)
+            outs.append((shard.mul_2_4_gathered(A, sw, gather), A, W))
+        gather.wait()
+        torch.cuda.synchronize()
+        C, A, W = outs[-1]
+        rel_mae, rel_fro, _ = errors(C, A.float() @ torch.from_numpy(W).to(DEV).float())
+        assert rel_mae < REL_MAE_TOL and rel_fro <= REL_FRO_TOL, (rel_mae, rel_fro)
+        assert m.device_status(0) == 0
+    finally:
+        gather.close()
+
+
+def _fused_worker(rank, world, port, q, pipelined):
     import datetime
 
     import torch.distributed as dist
@@ -125,7 +156,7 @@ def _fused_worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     dev = torch.device("cuda", rank)
-    gather = shard.FusedGather(16, 12288 // world, device=dev)
+    gather = shard.FusedGather(16, 12288 // world, device=dev, pipelined=pipelined)
     try:
         shapes = [(4096, 4096), (11008, 4096), (4096, 4096), (12288, 4096), (4096, 11008)]
         for i, (N, K) in enumerate(shapes):
@@ -134,6 +165,7 @@ def _fused_worker(rank, world, port, q):
                                      torch.from_numpy(s).to(dev), rank, world)
             A = torch.from_numpy(activations(16, K, seed=30 + i)).to(dev)
             C = shard.mul_2_4_gathered(A, sw, gather)
+            gather.wait()
             torch.cuda.synchronize(dev)
             rel_mae, rel_fro, _ = errors(C, A.float() @ torch.from_numpy(W).to(dev).float())
             q.put((rank, i, rel_mae, rel_fro))
@@ -144,14 +176,16 @@ def _fused_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_fused_gather_two_ranks():
+@pytest.mark.parametrize("pipelined", [True, False])
+def test_fused_gather_two_ranks(pipelined):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q, pipelined))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
