@@ -45,6 +45,8 @@ sys.path.insert(0, ROOT)
 
 LAYERS = 32
 SHAPES = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]  # (K, N)
+# one Llama-2-70B layer set (qkv, o, gate+up, down)
+SHAPES_70B = [(8192, 10240), (8192, 8192), (8192, 57344), (28672, 8192)]
 GROUP = 128
 # (batch rows, metadata bits) -> mean DRAM bytes per GEMM launch over SHAPES,
 # `dram__bytes_read.sum + dram__bytes_write.sum` from one ncu capture of the
@@ -150,20 +152,22 @@ def bench_ours(args, torch, dist, rank, world, dev):
 
     lib = m._ext.load()
     M = args.m
+    shapes = args.shapes
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    layers = [[make_layer(torch, K, N, dev, gen, args.meta_bits) for (K, N) in SHAPES]
+    layers = [[make_layer(torch, K, N, dev, gen, args.meta_bits) for (K, N) in shapes]
               for _ in range(args.layers)]
-    A = {K: torch.randn((M, K), dtype=torch.half, device=dev, generator=gen) for K in (4096, 11008)}
-    C = {N: torch.empty((M, N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
+    A = {K: torch.randn((M, K), dtype=torch.half, device=dev, generator=gen)
+         for K in sorted({K for K, _ in shapes})}
+    C = {N: torch.empty((M, N), dtype=torch.half, device=dev) for (_, N) in shapes}
     # N > 1: column-parallel layers of width world * N; this rank holds one
     # N-wide shard and every GEMM is followed by the all-gather of C
-    Cg = {N: torch.empty((M, world * N), dtype=torch.half, device=dev) for (_, N) in SHAPES}
+    Cg = {N: torch.empty((M, world * N), dtype=torch.half, device=dev) for (_, N) in shapes}
 
     def gather(N):
         if world > 1:
             shard.gather_columns(C[N], out=Cg[N])
-    ws = torch.zeros(22016 // 128 * 16, dtype=torch.int32, device=dev)
+    ws = torch.zeros(max(N for _, N in shapes) // 128 * 16, dtype=torch.int32, device=dev)
     devi = dev.index
     fn = lib.sm100_marlin_mul_2_4 if args.meta_bits == 4 else lib.sm100_marlin_mul_2_4_meta3
     stream = torch.cuda.Stream(device=dev)
@@ -174,14 +178,14 @@ def bench_ours(args, torch, dist, rank, world, dev):
     # are complete inside the timed region); --gather nccl: separate NCCL
     # all-gather after each GEMM
     fused = world > 1 and args.gather in ("fused", "fused-sync")
-    fg = (shard.FusedGather(M, max(N for _, N in SHAPES), device=dev,
+    fg = (shard.FusedGather(M, max(N for _, N in shapes), device=dev,
                             pipelined=args.gather == "fused") if fused else None)
     shards = [[shard.ShardedWeight.from_local(B, meta, s, rank * N, (rank + 1) * N, args.meta_bits)
-               for (K, N), (B, meta, s) in zip(SHAPES, lay)] for lay in layers] if fused else None
+               for (K, N), (B, meta, s) in zip(shapes, lay)] for lay in layers] if fused else None
 
     def step_raw(s_ptr):
         for li, lay in enumerate(layers):
-            for si, ((K, N), (B, meta, s)) in enumerate(zip(SHAPES, lay)):
+            for si, ((K, N), (B, meta, s)) in enumerate(zip(shapes, lay)):
                 if fused:
                     rc, _ = fg.issue(A[K].data_ptr(), B.data_ptr(), meta.data_ptr(), s.data_ptr(),
                                      N, M, K, shards[li][si].workspace.data_ptr(), GROUP // 2,
@@ -197,8 +201,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
         if fused:
             fg.wait(s_ptr)
 
-    bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in SHAPES)
-    launches_step = args.layers * len(SHAPES) * ((M + 63) // 64)
+    bytes_step = args.layers * sum(algo_bytes(M, K, N, args.meta_bits) for (K, N) in shapes)
+    launches_step = args.layers * len(shapes) * ((M + 63) // 64)
 
     # warm-up eagerly (sizes the split-K scratch before capture), then capture
     with torch.cuda.stream(stream):
@@ -239,7 +243,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
 
     # ---- per-shape kernel times (for the detail block), inputs resident
     detail = {}
-    for (K, N), idx in zip(SHAPES, range(4)):
+    for (K, N), idx in zip(shapes, range(len(shapes))):
         g2 = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g2, stream=stream):
             sp = torch.cuda.current_stream(dev).cuda_stream
@@ -281,7 +285,7 @@ def bench_ours(args, torch, dist, rank, world, dev):
         for K in A_h:
             A_d[K].copy_(A_h[K], non_blocking=True)
         for li, lay in enumerate(layers):
-            for si, ((K, N), (B, meta, s)) in enumerate(zip(SHAPES, lay)):
+            for si, ((K, N), (B, meta, s)) in enumerate(zip(shapes, lay)):
                 if fused:
                     C_out[N] = shard.mul_2_4_gathered(A_d[K], shards[li][si], fg)
                     continue
@@ -327,8 +331,8 @@ def bench_ours(args, torch, dist, rank, world, dev):
     # DRAM bytes (read + write) per launch from a separate ncu capture of the
     # same kernel and shapes, averaged over the four shapes like `achieved`;
     # only known for the default case.
-    traffic = MEASURED_TRAFFIC.get((M, args.meta_bits))
-    achieved = bytes_step / args.layers / len(SHAPES) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
+    traffic = MEASURED_TRAFFIC.get((M, args.meta_bits)) if shapes == SHAPES else None
+    achieved = bytes_step / args.layers / len(shapes) / (per_launch_us * 1e-6) / 1e9 if M <= 64 else None
     return dict(
         value=value, ms_step=ms_step, per_launch_us=per_launch_us, bytes_step=bytes_step,
         launches=launches_step * args.steps, clocks=clk.summary(), detail=detail,
@@ -682,10 +686,12 @@ def main():
                          "stores) with pipelined completion (each step ends with a wait for "
                          "its last exchange), the same with per-call completion, or a "
                          "separate NCCL all-gather")
-    ap.add_argument("--workload", choices=["decode", "prefill", "ablation"], default="decode",
-                    help="decode: Llama-2-7B decode step (config 1, the headline); "
-                         "prefill: compute-bound sweep (config 4); ablation: metadata-cost "
-                         "diagnostics (config 4's ablation)")
+    ap.add_argument("--workload", choices=["decode", "llama70b", "prefill", "ablation"],
+                    default="decode",
+                    help="decode: Llama-2-7B decode step (config 1, the headline; N > 1: weak "
+                         "scaling); llama70b: Llama-2-70B layer set (config 3), N-sharded across "
+                         "the ranks (strong scaling); prefill: compute-bound sweep (config 4); "
+                         "ablation: metadata-cost diagnostics (config 4's ablation)")
     ap.add_argument("--no-prefill-sample", action="store_true",
                     help="decode: skip the config-4 prefill sample in `detail`")
     ap.add_argument("--no-comparator", action="store_true",
@@ -697,6 +703,17 @@ def main():
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    strong = args.workload == "llama70b"
+    if strong:
+        if any(N % (128 * world) for _, N in SHAPES_70B):
+            raise SystemExit(f"llama70b: the layer widths do not split into {world} shards")
+        args.shapes = [(K, N // world) for (K, N) in SHAPES_70B]
+        if args.layers == LAYERS:
+            args.layers = 8  # 2.7 GB of weights per step on one GPU
+        args.no_cpu_baseline = True
+        args.no_prefill_sample = True
+    else:
+        args.shapes = SHAPES
     config = {"workload": f"Llama-2-7B decode step: {args.layers} layers x 4 GEMMs "
                           f"(K,N) in {SHAPES}, M={args.m}, 2:4 INT4 g128, {args.meta_bits}-bit meta",
               "model_shapes": "Llama-2-7B", "batch_rows": args.m, "groupsize": GROUP,
@@ -708,9 +725,27 @@ def main():
                               f"{args.gpus}N-wide layers (weak scaling), all-gather of C after "
                               f"every GEMM ({'fused into the GEMM epilogue over NVLink' if args.gather == 'fused' else 'NCCL'})")}
     metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-7B decode layer set, M={args.m})"
+    if strong:
+        layer_gb = sum(algo_bytes(args.m, K, N, args.meta_bits) for (K, N) in SHAPES_70B) / 1e9
+        config = {"workload": f"Llama-2-70B layer set: {args.layers} layers x 4 GEMMs (K,N) in "
+                              f"{SHAPES_70B}, M={args.m}, 2:4 INT4 g128, {args.meta_bits}-bit meta, "
+                              f"every layer's columns split over {world} ranks",
+                  "model_shapes": "Llama-2-70B", "batch_rows": args.m, "groupsize": GROUP,
+                  "meta_bits": args.meta_bits, "layers": args.layers,
+                  "l2": f"inputs larger than L2: {args.layers * layer_gb / world:.2f} GB of "
+                        f"weights per rank per step",
+                  "parallelism": ("single GPU" if world == 1 else
+                                  f"tp{world} column-parallel (strong scaling): each rank holds "
+                                  f"1/{world} of every layer's columns, all-gather of C after every "
+                                  f"GEMM ({args.gather})")}
+        metric = f"2:4 W4A16 GEMM HBM GB/s (Llama-2-70B layer set, M={args.m}, column-sharded)"
 
     if args.impl == "reference":
         if rank != 0:
+            return
+        if strong:
+            print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm times the "
+                              "Llama-2-7B decode workload only"}), flush=True)
             return
         ref = cpu_reference(args.m, args.meta_bits, reps=max(args.steps, 1))
         keys = ("value", "unit", "cores", "kind", "sample", "cpu_model", "os_cpu_count")
@@ -791,7 +826,8 @@ def main():
     if rank == 0:
         line = dict(metric=metric, value=round(res["value"], 2), unit="GB/s", n_gpus=world,
                     steps=args.steps, warmup=args.warmup, ms_per_step=round(res["ms_step"], 5),
-                    higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f16",
+                    higher_is_better=True, scaling="strong" if strong else "weak",
+                    vs_baseline=None, dtype="f16",
                     data="synthetic (random packed INT4 codes, random legal 2:4 metadata, "
                          "random fp16 group scales; seeded)",
                     config=config, e2e=res["e2e"], roofline=res["roofline"],
