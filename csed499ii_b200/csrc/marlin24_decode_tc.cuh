@@ -15,32 +15,34 @@
 // K S ways: CTA r of the cluster streams K steps [r*ks/S, (r+1)*ks/S) of every
 // block of the cluster, block after block.  The S partial sums of a block are
 // reduced through distributed shared memory: CTA r owns rows
-// [r*128/S, (r+1)*128/S) of every block, every CTA sends it those rows of its
-// partial (st.async, counted on the owner's mbarrier), and the owner adds the
-// S partials in rank order (deterministic) and stores its part of C.  No
-// global scratch, no split-K counters: the workspace is never touched.
+// [r*128/S, (r+1)*128/S) of every block, every other CTA sends it those rows
+// of its partial (st.async, counted on the owner's mbarrier; the owner's own
+// rows are plain shared-memory stores), and the owner adds the S partials in
+// rank order (deterministic) and stores its part of C.  No global scratch, no
+// split-K counters: the workspace is never touched.
 //
-// Warp roles (16 warps, one CTA per SM).  Every single-thread issue of a TMA
-// copy, barrier wait, MMA or commit costs ~100-200 cycles on B200, so stages
-// are 256 K deep (8 MMAs of K = 32 per 128-feature block) and the issuing
-// roles are doubled:
+// Warp roles (one CTA per SM).  Every single-thread issue of a TMA copy,
+// barrier wait, MMA or commit costs ~100-200 cycles on B200, so stages are
+// 256 K deep (8 MMAs of K = 32 per 128-feature block; 128 K for the 48- and
+// 64-row tiles, whose activation slices are larger) and the issuing roles are
+// doubled (the counts per tile are in DecodeTcCfg):
 //   warps 0-1    TMA, stages in turn: the packed codes, metadata and scale
 //                rows of the block (before the programmatic-launch wait:
 //                weights do not depend on the previous kernel), then the
 //                activation slice.
-//   warps 2-3    MMA issue (one thread each), a block's stages in turn, each
-//                into its own accumulator (the epilogue adds the two in a
+//   MMA_WARPS    MMA issue (one thread each), a block's stages in turn, each
+//                into its own accumulator (the epilogue adds them in a
 //                fixed order); tensor-memory allocation.
-//   warps 4-11   dequantise, two groups of four taking the stages in turn:
+//   4 x DG       dequantise, DG groups of four taking the stages in turn:
 //                each thread owns one MMA row (one output feature): INT4
 //                codes -> fp16 (magic-number method), group scale applied,
 //                the 16 compressed values of each 32-K row written to its
 //                tensor-memory lane (tcgen05.st), and its metadata word
 //                copied (3-bit metadata decoded first).
-//   warps 12-15  epilogue: accumulators -> registers, the DSMEM exchange,
+//   last 4       epilogue: accumulators -> registers, the DSMEM exchange,
 //                sums and the 16-byte stores of C.
-// Two accumulator pairs alternate between consecutive blocks, so the
-// epilogue of one block overlaps the MMAs of the next.
+// With two accumulator sets (16 and 32 rows) consecutive blocks alternate
+// between them, so the epilogue of one block overlaps the MMAs of the next.
 //
 // Row order.  MMA row m (tensor-memory lane m) of a block holds output feature
 // 32q + phi(l) of the block, q = m / 32, l = m % 32,
@@ -123,9 +125,15 @@ struct DecodeTcCfg {
   static constexpr int OFF_S = OFF_M + META;
   static constexpr int STAGE = (OFF_S + SCALES + 1023) / 1024 * 1024;
   static constexpr int HEADER = 1024;
+  // Accumulator (and exchange-buffer) sets.  Two let the epilogue of block j
+  // overlap the MMAs of block j + 1; the 48- and 64-row tiles keep one, which
+  // doubles their tensor-memory stages (4 -> 8 at 64 rows) and frees an
+  // exchange buffer for shared-memory stages (6 -> 8).  Measured on the
+  // Llama-7B step at 64 rows, with four dequantising groups: 1235 -> 1291 GB/s.
+  static constexpr int NACC = NR >= 48 ? 1 : 2;
   static constexpr int RECV = 128 * NR * 4;            // one exchange buffer
   static constexpr int OFF_RECV = HEADER;
-  static constexpr int OFF_RING = HEADER + 2 * RECV;
+  static constexpr int OFF_RING = HEADER + NACC * RECV;
   // MMA-issuing warps: a thread issues one tcgen05.mma per ~90-160 cycles
   // whatever N is, and separate warps issue in parallel, so the 16-row tile
   // (the least work per MMA) gets four, one per SM sub-partition.
@@ -133,8 +141,11 @@ struct DecodeTcCfg {
   // Dequantising groups of four warps (one per tensor-memory lane quarter).
   // The dequantisation is latency-bound (a warp issues ~0.25 instructions
   // per cycle), so the 16-row tile, whose stages carry the least MMA work,
-  // runs four groups.
-  static constexpr int DG = NR == 16 ? 4 : 2;
+  // runs four groups, and so do the 48- and 64-row tiles, whose 128-K stages
+  // and eight tensor-memory stages keep four groups busy.  The 32-row tile
+  // keeps two groups and 256-K stages (the 48/64-row configuration measured
+  // 1458 vs 1721 GB/s on its step).
+  static constexpr int DG = (NR == 16 || NR >= 48) ? 4 : 2;
   // Ring depths are multiples of every role's warp count (two TMA warps, DG
   // dequantising groups, MMA_WARPS MMA warps): each role takes stages in
   // turn, so each warp (group) then owns a fixed subset of the slots and
@@ -148,7 +159,7 @@ struct DecodeTcCfg {
   // tensor memory: per stage 8 MMAs x (8 A + 4 metadata) columns; two
   // accumulators (consecutive blocks) for each MMA-issuing warp
   static constexpr int TSLOT = KS * 48;
-  static constexpr int ACC_COLS = MMA_WARPS * 2 * NR;
+  static constexpr int ACC_COLS = MMA_WARPS * NACC * NR;
   static constexpr int DT_FIT = (TMEM_COLS - ACC_COLS) / TSLOT;
   static constexpr int DT_CAP = 4 * 2 / KS;  // at most 1024 K in tensor memory
   static constexpr int DT = (DT_FIT > DT_CAP ? DT_CAP : DT_FIT) / RING_MULT * RING_MULT;  // tensor-memory stages
@@ -158,6 +169,9 @@ struct DecodeTcCfg {
   static constexpr int WARP_DQ = WARP_MMA + MMA_WARPS;
   static constexpr int WARP_EPI = WARP_DQ + 4 * DG;
   static constexpr int THREADS = (WARP_EPI + 4) * 32;
+  // Epilogue columns read from tensor memory at a time: the whole row unless
+  // the register budget of a larger CTA (above 640 threads) forbids it.
+  static constexpr int EPI_CHUNK = (THREADS > 640 && NR > 16) ? 16 : NR;
   static_assert(DS >= RING_MULT && DT >= RING_MULT && DS % RING_MULT == 0 &&
                     DT % RING_MULT == 0 && DS % 2 == 0,
                 "ring depths");
@@ -222,9 +236,9 @@ __device__ __forceinline__ void sts128(uint32_t addr, const float4& v) {
                : "memory");
 }
 
-__device__ __forceinline__ float lds_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+__device__ __forceinline__ float2 lds_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
   return v;
 }
 
@@ -255,6 +269,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
   constexpr int DS = Cfg::DS;
   constexpr int DT = Cfg::DT;
   constexpr int KS = Cfg::KS;
+  constexpr int NACC = Cfg::NACC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -434,8 +449,8 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
         if ((s & (mma_warps - 1)) == w) {
           bool ok = true;
           stamp(s, 8);
-          if (first && j >= 2)  // the epilogue has read this accumulator out
-            ok = mbar_wait_spin_sleep_bounded(smem_addr(&accempty[j & 1]), ((j >> 1) - 1) & 1, abort_flag);
+          if (first && j >= NACC)  // the epilogue has read this accumulator out
+            ok = mbar_wait_spin_sleep_bounded(smem_addr(&accempty[j % NACC]), ((j / NACC) - 1) & 1, abort_flag);
           ok = ok && mbar_wait_spin_sleep_bounded(smem_addr(&tready[t]), tph, abort_flag);
           stamp(s, 9);
           ok = ok && mbar_wait_spin_sleep_bounded(smem_addr(&afull[slot]), sph, abort_flag);
@@ -448,7 +463,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
           tc_fence_after();
           stamp(s, 3);
           if (lane == 0) {
-            const uint32_t acc = tmem + (w * 2 + (j & 1)) * NR;
+            const uint32_t acc = tmem + (w * NACC + j % NACC) * NR;
             const uint32_t ta = tmem + Cfg::ACC_COLS + t * Cfg::TSLOT;
             const uint64_t bd = umma_desc_sw128_k(ring + slot * Cfg::STAGE + Cfg::OFF_ACT);
 #pragma unroll
@@ -460,7 +475,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
             umma_commit(smem_addr(&tempty[t]));
             umma_commit(smem_addr(&sempty[slot]));
             // this warp's last stage of the block
-            if (i_in + mma_warps >= kn) umma_commit(smem_addr(&accfull[j & 1]));
+            if (i_in + mma_warps >= kn) umma_commit(smem_addr(&accfull[j % NACC]));
           }
           stamp(s, 4);
           __syncwarp();
@@ -604,8 +619,9 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
     if (S > 1) cluster_wait();
     if (trace && et == 0) trace[kTcTraceWords * kTcTraceStages + 5] = clock64();
     for (int j = 0; j < nb; ++j) {
-      const int buf = j & 1;
-      bool ok = mbar_wait_spin_sleep_bounded(smem_addr(&accfull[buf]), (j >> 1) & 1, abort_flag);
+      const int buf = j % NACC;
+      const uint32_t par = static_cast<uint32_t>(j / NACC) & 1u;
+      bool ok = mbar_wait_spin_sleep_bounded(smem_addr(&accfull[buf]), par, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) atomicOr(p.status, kStatusFullWaitTimeout);
         break;
@@ -613,106 +629,143 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
       tc_fence_after();
       if (q == 0) stamp(j * kn, 5);
       if (j == nb - 1 && et == 0) gstamp(5);
-      // sum of the MMA warps' accumulators, warp 0 first
-      uint32_t r[NR];
-      float acc[NR];
-#pragma unroll
-      for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + buf * NR + c0, r + c0);
-      tmem_wait_ld();
-#pragma unroll
-      for (int u = 0; u < NR; ++u) acc[u] = __uint_as_float(r[u]);
-      for (int w = 1; w < mma_warps; ++w) {
-#pragma unroll
-        for (int c0 = 0; c0 < NR; c0 += 16) tmem_ld16(lane_acc + (2 * w + buf) * NR + c0, r + c0);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < NR; ++u) acc[u] += __uint_as_float(r[u]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&accempty[buf]));
-      // every owner has released exchange buffer `buf` (block j - 2)
-      if (S > 1 && j >= 2) {
-        ok = mbar_wait_sleep_bounded(smem_addr(&freeb[buf]), ((j >> 1) - 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) {
-          if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
-          break;
-        }
-      }
       // this row of the partial -> its owner's buffer, at [rank][feature in slice]
       const uint32_t dst = recv + buf * Cfg::RECV +
                            ((rank * slice + (feat - static_cast<int>(owner) * slice)) * NR) * 4;
-      if (S > 1) {
-        const uint32_t rdst = mapa_shared(dst, owner);
-        const uint32_t rbar = mapa_shared(smem_addr(&recvb[buf]), owner);
+      const uint32_t rdst = S > 1 ? mapa_shared(dst, owner) : dst;
+      const uint32_t rbar = S > 1 ? mapa_shared(smem_addr(&recvb[buf]), owner) : 0u;
+      // The sum of the MMA warps' accumulators (warp 0 first), ECH columns at
+      // a time: the accumulators are released after the last chunk is read,
+      // and exchange buffer `buf` must be free (all owners done with block
+      // j - NACC) before the first chunk is sent.
+      constexpr int ECH = Cfg::EPI_CHUNK;
+      bool failed = false;
 #pragma unroll
-        for (int c0 = 0; c0 < NR; c0 += 4)
-          st_async_v4(rdst + 4 * c0, make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]), rbar);
+      for (int e0 = 0; e0 < NR; e0 += ECH) {
+        uint32_t r[ECH];
+        float acc[ECH];
+#pragma unroll
+        for (int c0 = 0; c0 < ECH; c0 += 16) tmem_ld16(lane_acc + buf * NR + e0 + c0, r + c0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < ECH; ++u) acc[u] = __uint_as_float(r[u]);
+        for (int w = 1; w < mma_warps; ++w) {
+#pragma unroll
+          for (int c0 = 0; c0 < ECH; c0 += 16)
+            tmem_ld16(lane_acc + (NACC * w + buf) * NR + e0 + c0, r + c0);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < ECH; ++u) acc[u] += __uint_as_float(r[u]);
+        }
+        if (e0 + ECH == NR) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&accempty[buf]));
+        }
+        if (e0 == 0 && S > 1 && j >= NACC) {
+          ok = mbar_wait_sleep_bounded(smem_addr(&freeb[buf]), (par - 1u) & 1u, abort_flag);
+          if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
+            failed = true;
+            break;
+          }
+        }
+        if (owner != rank) {  // warp-uniform: a warp's 32 rows have one owner
+#pragma unroll
+          for (int c0 = 0; c0 < ECH; c0 += 4)
+            st_async_v4(rdst + 4 * (e0 + c0), make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]),
+                        rbar);
+        } else {
+#pragma unroll
+          for (int c0 = 0; c0 < ECH; c0 += 4)
+            sts128(dst + 4 * (e0 + c0), make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]));
+        }
+      }
+      if (failed) break;
+      if (S > 1) {
         if (q == 0) stamp(j * kn, 11);
-        if (et == 0) mbar_arrive_expect_tx(smem_addr(&recvb[buf]), Cfg::RECV);
-        ok = mbar_wait_spin_sleep_bounded(smem_addr(&recvb[buf]), (j >> 1) & 1, abort_flag);
+        // the peers' slices; this CTA's own slice was stored locally (ordered
+        // by the named barrier below)
+        if (et == 0) mbar_arrive_expect_tx(smem_addr(&recvb[buf]), Cfg::RECV - Cfg::RECV / S);
+        ok = mbar_wait_spin_sleep_bounded(smem_addr(&recvb[buf]), par, abort_flag);
         if (q == 0) stamp(j * kn, 12);
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) atomicOr(p.status, kStatusFinishWaitTimeout);
           break;
         }
-      } else {
-#pragma unroll
-        for (int c0 = 0; c0 < NR; c0 += 4)
-          sts128(dst + 4 * c0, make_float4(acc[c0], acc[c0 + 1], acc[c0 + 2], acc[c0 + 3]));
       }
       named_bar_sync(1, 128);
-      // sums of this CTA's slice: 8 features x 1 batch row per item, the S
-      // partials added in rank order; 16-byte stores of C
+      // sums of this CTA's slice: 8 features x 2 batch rows per item, the S
+      // partials added in rank order; 16-byte stores of C.  Lanes take
+      // consecutive row pairs of one feature group, so each warp-wide 8-byte
+      // load reads one contiguous run of the buffer (no bank conflicts).
       const int n0 = (b0 + j) * 128 + static_cast<int>(rank) * slice;
       const int groups = slice / 8;
-      for (int it = et; it < groups * p.M; it += 128) {
-        const int rr = it / groups;
-        const int fg = it - rr * groups;
-        float sum[8];
+      const int pairs = (p.M + 1) >> 1;
+      for (int it = et; it < groups * pairs; it += 128) {
+        const int fg = it / pairs;
+        const int rp = it - fg * pairs;
+        float sum[2][8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) sum[u] = 0.f;
+        for (int u = 0; u < 8; ++u) sum[0][u] = sum[1][u] = 0.f;
         for (int src = 0; src < S; ++src) {
-          const uint32_t base = recv + buf * Cfg::RECV + ((src * slice + fg * 8) * NR + rr) * 4;
+          const uint32_t base = recv + buf * Cfg::RECV + ((src * slice + fg * 8) * NR + 2 * rp) * 4;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) sum[u] += lds_f32(base + u * NR * 4);
+          for (int u = 0; u < 8; ++u) {
+            const float2 v = lds_f32x2(base + u * NR * 4);
+            sum[0][u] += v.x;
+            sum[1][u] += v.y;
+          }
         }
         const int n = n0 + fg * 8;
+        float sc[8], bv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          sc[u] = 1.f;
+          bv[u] = 0.f;
+        }
         if (!GROUPED) {
           const uint4 sv = *reinterpret_cast<const uint4*>(p.s + 2ll * n);
           const half2* sh = reinterpret_cast<const half2*>(&sv);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            sum[2 * u] *= __low2float(sh[u]);
-            sum[2 * u + 1] *= __high2float(sh[u]);
+            sc[2 * u] = __low2float(sh[u]);
+            sc[2 * u + 1] = __high2float(sh[u]);
           }
         }
-        if (p.bias != nullptr || p.act != kActNone) {
-          float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (p.bias != nullptr) {
-            const uint4 braw = *reinterpret_cast<const uint4*>(p.bias + n);
-            const half2* bh = reinterpret_cast<const half2*>(&braw);
+        const bool fused = p.bias != nullptr || p.act != kActNone;
+        if (p.bias != nullptr) {
+          const uint4 braw = *reinterpret_cast<const uint4*>(p.bias + n);
+          const half2* bh = reinterpret_cast<const half2*>(&braw);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              bv[2 * u] = __low2float(bh[u]);
-              bv[2 * u + 1] = __high2float(bh[u]);
-            }
+          for (int u = 0; u < 4; ++u) {
+            bv[2 * u] = __low2float(bh[u]);
+            bv[2 * u + 1] = __high2float(bh[u]);
           }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) sum[u] = epilogue_act(sum[u] + bv[u], p.act);
         }
-        uint4 o;
-        half2* oh = reinterpret_cast<half2*>(&o);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) oh[u] = __floats2half2_rn(sum[2 * u], sum[2 * u + 1]);
-        *reinterpret_cast<uint4*>(p.C + static_cast<long long>(rr) * p.N + n) = o;
+        for (int h = 0; h < 2; ++h) {
+          const int rr = 2 * rp + h;
+          if (rr >= p.M) break;
+          float o8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            o8[u] = GROUPED ? sum[h][u] : sum[h][u] * sc[u];
+            if (fused) o8[u] = epilogue_act(o8[u] + bv[u], p.act);
+          }
+          uint4 o;
+          half2* oh = reinterpret_cast<half2*>(&o);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) oh[u] = __floats2half2_rn(o8[2 * u], o8[2 * u + 1]);
+          *reinterpret_cast<uint4*>(p.C + static_cast<long long>(rr) * p.N + n) = o;
+        }
       }
       named_bar_sync(1, 128);
       if (q == 0) stamp(j * kn, 6);
       if (j == nb - 1 && et == 0) gstamp(6);
       // release buffer `buf` to every CTA of the cluster (needed only when a
-      // block j + 2 follows)
-      if (S > 1 && j + 2 < nb && et < S)
+      // block j + NACC follows)
+      if (S > 1 && j + NACC < nb && et < S)
         mbar_arrive_remote(mapa_shared(smem_addr(&freeb[buf]), static_cast<uint32_t>(et)));
     }
   }
@@ -720,7 +773,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
   // Teardown: all MMAs complete before the tensor memory is released.  No
   // cluster barrier: every remote write aimed at a CTA (its peers' st.async
   // partials, counted on its recvb, and their freeb arrivals, which it waits
-  // for before its exchange of block j + 2) precedes a wait that the CTA has
+  // for before its exchange of block j + NACC) precedes a wait that the CTA has
   // passed by the end of its last exchange, so a CTA may leave as soon as it
   // is done.  Each thread completes its start-up cluster arrival.
   if (S > 1 && warp < Cfg::WARP_EPI) cluster_wait();
@@ -728,7 +781,7 @@ __global__ void __launch_bounds__(DecodeTcCfg<NR, META3>::THREADS, 1)
   __syncthreads();
   if (warp == Cfg::WARP_MMA) {
     if (*abort_flag == 0)  // the last block's accumulators are complete
-      mbar_wait_sleep_bounded(smem_addr(&accfull[(nb - 1) & 1]), ((nb - 1) >> 1) & 1, abort_flag);
+      mbar_wait_sleep_bounded(smem_addr(&accfull[(nb - 1) % NACC]), ((nb - 1) / NACC) & 1, abort_flag);
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
