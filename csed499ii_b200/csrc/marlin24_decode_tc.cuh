@@ -126,18 +126,21 @@ struct DecodeTcCfg {
   static constexpr int STAGE = (OFF_S + SCALES + 1023) / 1024 * 1024;
   static constexpr int HEADER = 1024;
   // Accumulator (and exchange-buffer) sets.  Two let the epilogue of block j
-  // overlap the MMAs of block j + 1; the 48- and 64-row tiles keep one, which
-  // doubles their tensor-memory stages (4 -> 8 at 64 rows) and frees an
-  // exchange buffer for shared-memory stages (6 -> 8).  Measured on the
-  // Llama-7B step at 64 rows, with four dequantising groups: 1235 -> 1291 GB/s.
+  // overlap the MMAs of block j + 1; the 48- and 64-row tiles keep one, so
+  // that four MMA warps' accumulators still leave four tensor-memory stages,
+  // and the freed exchange buffer deepens the shared-memory ring (6 -> 8).
   static constexpr int NACC = NR >= 48 ? 1 : 2;
   static constexpr int RECV = 128 * NR * 4;            // one exchange buffer
   static constexpr int OFF_RECV = HEADER;
   static constexpr int OFF_RING = HEADER + NACC * RECV;
   // MMA-issuing warps: a thread issues one tcgen05.mma per ~90-160 cycles
   // whatever N is, and separate warps issue in parallel, so the 16-row tile
-  // (the least work per MMA) gets four, one per SM sub-partition.
-  static constexpr int MMA_WARPS = NR == 16 ? 4 : 2;
+  // (the least work per MMA) gets four, one per SM sub-partition.  So do the
+  // 48- and 64-row tiles: their 128-K stages carry four MMAs and two barrier
+  // waits and two commits each (~1400 cycles of one thread per stage in a
+  // trace with two MMA warps, which set the stage rate); four warps took the
+  // 64-row step from 1391 to 1474 GB/s.
+  static constexpr int MMA_WARPS = (NR == 16 || NR >= 48) ? 4 : 2;
   // Dequantising groups of four warps (one per tensor-memory lane quarter).
   // The dequantisation is latency-bound (a warp issues ~0.25 instructions
   // per cycle), so the 16-row tile, whose stages carry the least MMA work,
